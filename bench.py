@@ -1,0 +1,326 @@
+"""Benchmark of the B200 token sampler on the north-star headline workload.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (per GPU, weak scaling): B=256 rows x V=151936 fp32 logits ``randn*3``,
+T=0.7, top-k 50, top-p 0.9, repetition 1.1, presence 0.5, frequency 0.3, 1024
+uniform history ids per row, one caller uniform per row (synthetic, seeded; the
+reference publishes no benchmark data).
+
+One step = one ``ns_sample`` launch over one batch.  ``value`` is sampled
+tokens/s over all ranks with inputs resident in HBM, timed with CUDA events
+around a CUDA-graph replay of K launches that rotate over 3 logits buffers
+(467 MB in total, > the 126 MB L2), max over ranks.  ``e2e`` is the same
+metric through the public ``B200Sampler.select_batch`` call with the logits
+in pinned host memory and the histories as Python lists (H2D copies, packing
+and the ids' D2H read inside the timed region).
+
+``--impl reference`` times the CPU restatement of the reference sampler
+(``oracle/``) on the host cores, on a bounded sample of rows per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "nano-inference_b200"))
+sys.path.insert(0, REPO)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "sampled tokens/sec and logits HBM GB/s vs peak at B=256,V=151936"
+UNIT = "tokens/s"
+N_BUFFERS = 3
+
+
+def _peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def algorithmic_bytes(B: int, V: int, H: int, esz: int = 4) -> int:
+    """Logits once + history ids + 36 B/row (6 fp32 params, uniform, int64 id)."""
+    return B * V * esz + B * H * 4 + B * 36
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path:
+            return None
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            for line in open(self.path):
+                f = [v.strip() for v in line.split(",")]
+                if len(f) < 9:
+                    continue
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+                for n, v in zip(names, f[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        except Exception:
+            return None
+        finally:
+            try:
+                os.unlink(self.path)
+            except OSError:
+                pass
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(world, v: float) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# CPU arm: the oracle restatement of the reference sampler
+# ---------------------------------------------------------------------------
+def cpu_port_tokens_per_s(w, rows: int, steps: int = 1, threads: int = 1):
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import sampler_oracle as O
+    x = w.logits.numpy()
+    u = w.uniforms.numpy()
+
+    def one(b):
+        return O.sample_row(x[b], w.histories[b], w.params[b], float(u[b])).token
+
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        if threads > 1:
+            with ThreadPoolExecutor(threads) as ex:
+                list(ex.map(one, range(rows)))
+        else:
+            for b in range(rows):
+                one(b)
+    dt = time.perf_counter() - t0
+    return rows * steps / dt, dt
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    from b200_sampler.workloads import headline
+    w = headline()
+    threads = os.cpu_count() or 1
+    # size the per-step sample so the whole run stays within about two minutes
+    probe_rate, _ = cpu_port_tokens_per_s(w, 2, 1, 1)
+    total_steps = args.steps + args.warmup
+    rows = int(max(1, min(w.batch, probe_rate * max(threads // 2, 1) * 100.0 / max(total_steps, 1))))
+    for _ in range(args.warmup):
+        cpu_port_tokens_per_s(w, rows, 1, threads)
+    rate, dt = cpu_port_tokens_per_s(w, rows, args.steps, threads)
+    cfg = {"workload": w.notes, "sample_rows_per_step": rows, "rows_per_step_full": w.batch}
+    line = {"impl": "reference", "metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3 * w.batch / rows,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded randn*3 logits, uniform histories)", "config": cfg,
+            "cpu_baseline": {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{rows} of {w.batch} rows of the headline workload per step, "
+                                       f"numpy restatement of Sampler.select_batch, {threads} threads"},
+            "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_ours(args, world, rank, local):
+    from b200_sampler import B200Sampler
+    from b200_sampler.sampler import DeviceBatch
+    from b200_sampler.workloads import headline
+
+    dev = torch.device("cuda", local)
+    w = headline(seed=rank)
+    B, V, H = w.batch, w.vocab, w.history_len
+    db = DeviceBatch(w.histories, w.params, dev, uniforms=w.uniforms)
+    bufs = [w.logits.to(dev)]
+    for i in range(1, N_BUFFERS):
+        bufs.append((w.logits.roll(i, dims=1)).to(dev))
+    out = torch.empty(B, dtype=torch.int64, device=dev)
+    stream = torch.cuda.Stream(dev)
+
+    # correctness gate on the benchmarked inputs (first rows only)
+    with torch.cuda.stream(stream):
+        rc = db.launch(bufs[0], out, stream)
+    stream.synchronize()
+    assert rc == 0, rc
+    assert int(out.min()) >= 0, "a row failed"
+
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            assert db.launch(bufs[i % N_BUFFERS], out, stream) == 0
+    stream.synchronize()
+
+    # one CUDA graph with K launches rotating over the buffers
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(args.steps):
+            db.launch(bufs[i % N_BUFFERS], out, torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        g.replay()                                   # graph warm-up
+    stream.synchronize()
+
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clk:
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+        stream.synchronize()
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    ms_max = max_over_ranks(world, ms)
+    ms_per_step = ms_max / args.steps
+    tokens_per_s = B * world / (ms_per_step / 1e3)
+
+    peak, peak_kind = _peaks()
+    alg = algorithmic_bytes(B, V, H)
+    achieved = alg / (ms / args.steps / 1e3) / 1e9
+    del g
+
+    # ---- end to end through the public API, host buffers ----
+    sampler = B200Sampler(device=dev, seed=1)
+    host_logits = w.logits.pin_memory()
+    hists = w.histories
+    u_host = w.uniforms
+    e2e_steps = max(1, min(args.steps, 10))
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            sampler.select_batch(host_logits, hists, w.params, uniforms=u_host)
+        barrier(world)
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            ids = sampler.select_batch(host_logits, hists, w.params, uniforms=u_host)
+        dt = time.perf_counter() - t0
+    dt = max_over_ranks(world, dt)
+    assert len(ids) == B
+    e2e = {"value": B * world * e2e_steps / dt, "unit": UNIT,
+           "h2d_bytes_per_step": B * V * 4 + B * H * 4 + (B + 1) * 8 + B * 24 + B * 4,
+           "d2h_bytes_per_step": B * 8, "steps": e2e_steps,
+           "path": "B200Sampler.select_batch(pinned host logits, List[List[int]] histories) -> List[int]"}
+
+    line = {"metric": METRIC, "value": tokens_per_s, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded randn*3 logits, uniform histories)",
+            "config": {"workload": w.notes, "global_batch": B * world, "rows_per_gpu": B, "vocab": V,
+                       "parallelism": f"rows sharded, {world} GPU(s), no collective",
+                       "l2": f"{N_BUFFERS} rotating logits buffers ({N_BUFFERS * B * V * 4 / 1e6:.0f} MB) > L2",
+                       "timing": "CUDA graph of K launches, CUDA events, max over ranks"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": alg},
+            "gpu_launches": args.steps,
+            "e2e": e2e}
+    clocks = clk.summary()
+    if clocks is not None:
+        line["clocks"] = clocks
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, dtc = cpu_port_tokens_per_s(w, 8, 1, 1)
+        line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": 1, "kind": "port",
+                                "sample": "8 of 256 rows of the headline workload, numpy restatement of "
+                                          "Sampler.select_batch, 1 thread"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
+                          int(os.environ.get("LOCAL_RANK", "0")))
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,107 @@
+/*
+ * ns_sampler.h -- C ABI of the B200-native token sampler.
+ *
+ * Drop-in for the sampling step of apollo722/nano-inference:
+ *   Sampler.select_batch   src/nano_inference/sampling/sampler.py:36-91
+ *   Sampler.select         src/nano_inference/sampling/sampler.py:11-34
+ *   SamplerBase            src/nano_inference/sampling/base.py:10-25
+ * The reference is pure Python over torch; its "FFI" for this path is the
+ * Python call above.  A host binding (ctypes) passes device pointers taken from
+ * torch tensors plus the current CUDA stream; nothing here uses torch types.
+ *
+ * Conventions
+ *   - All pointers are DEVICE pointers unless stated otherwise.
+ *   - Every call is asynchronous on `stream` and returns an ns_status (0 = ok)
+ *     for argument / launch errors.  Errors found on the device (bad token id,
+ *     NaN/inf probabilities, capacity overflow) are written per row into the
+ *     output: out_ids[b] < 0 is the (negative) ns_status of row b.
+ *   - The sampler never writes the logits (the reference mutates them in place
+ *     at sampler.py:52; no caller depends on it).
+ *   - Kernels are re-entrant and keep no state between calls.
+ */
+#ifndef NS_SAMPLER_H
+#define NS_SAMPLER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t (struct CUstream_st*). */
+typedef struct CUstream_st* ns_stream_t;
+
+typedef enum ns_status {
+    NS_OK = 0,
+    NS_ERR_INVALID_ARGUMENT = -1,
+    NS_ERR_WORKSPACE_TOO_SMALL = -2,
+    NS_ERR_UNSUPPORTED_DTYPE = -3,
+    NS_ERR_CUDA = -4,
+    NS_ERR_DEVICE_TIMEOUT = -5,        /* a bounded device-side wait gave up */
+    NS_ERR_TOKEN_ID_OUT_OF_RANGE = -6, /* reference: IndexError at sampler.py:104 */
+    NS_ERR_INVALID_DISTRIBUTION = -7,  /* NaN / +inf / all -inf in a sampled row;
+                                          reference: torch.multinomial raises */
+    NS_ERR_HISTORY_TOO_LONG = -8,      /* more distinct history ids than the
+                                          per-block table holds */
+    NS_ERR_CANDIDATE_OVERFLOW = -9,    /* ties at a top-k threshold exceed the
+                                          candidate buffers */
+    NS_ERR_UNSUPPORTED = -10
+} ns_status;
+
+typedef enum ns_dtype {
+    NS_DTYPE_F32 = 0,
+    NS_DTYPE_BF16 = 1,   /* widened to fp32 exactly, as the engine's .float() */
+    NS_DTYPE_F16 = 2
+} ns_dtype;
+
+/* Human-readable text for an ns_status.  Never NULL. */
+const char* ns_status_string(int status);
+
+/* ABI version (major * 100 + minor). */
+int ns_version(void);
+
+/*
+ * Scratch bytes ns_sample needs for this problem size (may be 0).
+ * Replaces: nothing (the reference allocates per call inside torch ops).
+ */
+int ns_sampler_workspace_bytes(int64_t batch, int64_t vocab, int64_t max_history,
+                               size_t* out_bytes);
+
+/*
+ * Sample one token per row.
+ * Replaces: Sampler.select_batch (sampler.py:36-91), including
+ *   _apply_repetition_penalty (sampler.py:93-108), greedy argmax (:60-70),
+ *   temperature (:73-76), _apply_top_k_top_p (:110-133) and the
+ *   softmax + multinomial draw (:86-89), which becomes an inverse-CDF draw.
+ *
+ * logits        [batch, row_stride] of `dtype`; only the first `vocab`
+ *               columns of each row are read.  Element-aligned; 16-byte
+ *               aligned rows are the fast path.
+ * hist_ids      int32 token ids, CSR by row (prompt + outputs, duplicates
+ *               allowed; context_builder.py:208-213).  May be NULL.
+ * hist_offsets  int64 [batch + 1] row offsets into hist_ids.  May be NULL.
+ * max_history   host-side upper bound on any row's history length.
+ * temperature   fp32 [batch]; 0 => greedy.  (SamplingParams.temperature)
+ * top_k         int32 [batch]; active iff 0 < k < vocab.
+ * top_p         fp32 [batch]; active iff 0 < p < 1.
+ * repetition_penalty, presence_penalty, frequency_penalty
+ *               fp32 [batch] each, or NULL for 1.0 / 0.0 / 0.0.
+ * uniforms      fp32 [batch] in [0,1), one draw per row; if NULL the kernel
+ *               draws Philox4x32-10(counter = (row, philox_offset),
+ *               key = philox_seed).
+ * out_ids       int64 [batch]: sampled token id, or a negative ns_status.
+ */
+int ns_sample(const void* logits, int dtype, int64_t batch, int64_t vocab, int64_t row_stride,
+              const int32_t* hist_ids, const int64_t* hist_offsets, int64_t max_history,
+              const float* temperature, const int32_t* top_k, const float* top_p,
+              const float* repetition_penalty, const float* presence_penalty,
+              const float* frequency_penalty,
+              const float* uniforms, uint64_t philox_seed, uint64_t philox_offset,
+              int64_t* out_ids, void* workspace, size_t workspace_bytes, ns_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NS_SAMPLER_H */

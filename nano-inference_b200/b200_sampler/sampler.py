@@ -1,0 +1,285 @@
+"""``B200Sampler``: drop-in replacement for nano-inference's ``Sampler``.
+
+Keeps the reference call signature (``src/nano_inference/sampling/base.py:10-25``)::
+
+    select(logits, generated_ids, sampling_params) -> int
+    select_batch(logits, all_generated_ids, all_sampling_params) -> List[int]
+
+and the engine's keyword call (``inferencer/torch_inferencer.py:254-258``), so
+``inferencer.sampler = B200Sampler()`` is the whole integration.  Every row is
+sampled on the GPU by the CUDA library behind ``include/ns_sampler.h``; the
+host side only packs parameters and histories and reads back the ids.
+
+Differences from the reference, all documented in the C header:
+
+* the draw is an inverse-CDF draw from one uniform per row (caller supplied via
+  ``uniforms=``, else a Philox4x32-10 stream keyed by ``seed``), not
+  ``torch.multinomial``;
+* ``presence_penalty`` / ``frequency_penalty`` are honoured when present on the
+  params objects (default 0.0 reproduces the reference);
+* the caller's logits are not modified (the reference penalises them in place,
+  ``sampler.py:52``);
+* a negative history id is an error (the reference's Python indexing wraps it).
+"""
+from __future__ import annotations
+
+import itertools
+import threading
+from typing import List, Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import _lib
+from .params import pack_params
+
+try:  # the reference's ABC when nano-inference is installed
+    from nano_inference.sampling.base import SamplerBase  # type: ignore
+except Exception:  # pragma: no cover - mirror of sampling/base.py:10-25
+    from abc import ABC, abstractmethod
+
+    class SamplerBase(ABC):
+        @abstractmethod
+        def select(self, logits: torch.Tensor, generated_ids: List[int], sampling_params) -> int: ...
+
+        @abstractmethod
+        def select_batch(self, logits: torch.Tensor, all_generated_ids: List[List[int]],
+                         all_sampling_params) -> List[int]: ...
+
+
+_DTYPES = {torch.float32: _lib.NS_DTYPE_F32, torch.bfloat16: _lib.NS_DTYPE_BF16,
+           torch.float16: _lib.NS_DTYPE_F16}
+
+_ROW_ERRORS = {
+    _lib.NS_ERR_TOKEN_ID_OUT_OF_RANGE: IndexError,
+}
+
+
+def _align(n: int, a: int = 16) -> int:
+    return (n + a - 1) // a * a
+
+
+class _Staging:
+    """Pinned host block + device block for one call's small inputs (params,
+    history CSR, uniforms), uploaded with a single H2D copy."""
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.host = torch.empty(0, dtype=torch.uint8)
+        self.dev = torch.empty(0, dtype=torch.uint8, device=device)
+        self.event: Optional[torch.cuda.Event] = None
+
+    def reserve(self, nbytes: int):
+        if self.event is not None:
+            self.event.synchronize()      # previous upload has left the host block
+        if self.host.numel() < nbytes:
+            cap = max(nbytes, 2 * self.host.numel(), 1 << 16)
+            self.host = torch.empty(cap, dtype=torch.uint8, pin_memory=True)
+            self.dev = torch.empty(cap, dtype=torch.uint8, device=self.device)
+        return self.host.numpy()
+
+    def upload(self, nbytes: int, stream: torch.cuda.Stream):
+        with torch.cuda.stream(stream):
+            self.dev[:nbytes].copy_(self.host[:nbytes], non_blocking=True)
+            if self.event is None:
+                self.event = torch.cuda.Event()
+            self.event.record(stream)
+        return self.dev.data_ptr()
+
+
+class B200Sampler(SamplerBase):
+    """GPU sampler with the reference ``SamplerBase`` interface.
+
+    Args:
+        device: CUDA device for host-side inputs (default: the logits' device,
+            else the current device).
+        seed: Philox key for the default uniform stream.  Each call advances
+            the stream's offset by one.
+    """
+
+    def __init__(self, device=None, seed: Optional[int] = None):
+        self.lib = _lib.load()
+        if not torch.cuda.is_available():
+            raise RuntimeError("B200Sampler needs a CUDA device (there is no CPU fallback)")
+        self.device = torch.device(device) if device is not None else None
+        if seed is None:
+            seed = int(torch.initial_seed()) & 0xFFFFFFFFFFFFFFFF
+        self.seed = int(seed) & 0xFFFFFFFFFFFFFFFF
+        self.offset = 0
+        self._staging = {}
+        self._lock = threading.Lock()
+
+    # ------------------------------------------------------------------ API
+    def select(self, logits: torch.Tensor, generated_ids: List[int], sampling_params,
+               *, uniforms: Optional[torch.Tensor] = None) -> int:
+        """Single-row sampling (reference ``Sampler.select``, sampler.py:11-34)."""
+        if logits.dim() != 1:
+            raise ValueError("select expects a 1-D logits row")
+        u = None if uniforms is None else torch.as_tensor(uniforms, dtype=torch.float32).reshape(1)
+        return self.select_batch(logits.unsqueeze(0), [generated_ids], [sampling_params], uniforms=u)[0]
+
+    def select_batch(self, logits: torch.Tensor, all_generated_ids: List[List[int]],
+                     all_sampling_params, *, uniforms: Optional[torch.Tensor] = None) -> List[int]:
+        """Batch sampling (reference ``Sampler.select_batch``, sampler.py:36-91)."""
+        ids = self.select_batch_tensor(logits, all_generated_ids, all_sampling_params, uniforms=uniforms)
+        out = ids.tolist()
+        bad = [v for v in out if v < 0]
+        if bad:
+            code = int(bad[0])
+            exc = _ROW_ERRORS.get(code, RuntimeError)
+            raise exc(_lib.status_string(code))
+        return out
+
+    def select_batch_tensor(self, logits: torch.Tensor, all_generated_ids: Optional[Sequence[Sequence[int]]],
+                            all_sampling_params, *, uniforms: Optional[torch.Tensor] = None,
+                            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Like ``select_batch`` but asynchronous: returns int64 ids on the
+        device (a negative entry is the ns_status of a failed row)."""
+        if logits.dim() != 2:
+            raise ValueError("select_batch expects [batch, vocab] logits")
+        B, V = int(logits.shape[0]), int(logits.shape[1])
+        if all_generated_ids is not None and len(all_generated_ids) != B:
+            raise AssertionError("batch size mismatch (histories)")
+        if len(all_sampling_params) != B:
+            raise AssertionError("batch size mismatch (params)")
+        if logits.dtype not in _DTYPES:
+            raise TypeError(f"unsupported logits dtype {logits.dtype}")
+        device = self._device_for(logits)
+        if logits.device != device:
+            logits = logits.to(device, non_blocking=True)
+        if logits.stride(1) != 1:
+            logits = logits.contiguous()
+        stream = torch.cuda.current_stream(device)
+        if out is None:
+            out = torch.empty(B, dtype=torch.int64, device=device)
+        if B == 0:
+            return out
+
+        params = pack_params(all_sampling_params)                       # [6, B] 32-bit
+        use_hist = all_generated_ids is not None and bool(
+            (params[3] != 1.0).any() or (params[4] != 0.0).any() or (params[5] != 0.0).any())
+        if use_hist:
+            lens = np.fromiter((len(h) for h in all_generated_ids), dtype=np.int64, count=B)
+            total = int(lens.sum())
+            max_hist = int(lens.max()) if B else 0
+        else:
+            total, max_hist = 0, 0
+        host_u = uniforms is not None and uniforms.device.type == "cpu"
+
+        off_params = 0
+        off_offsets = _align(6 * B * 4)
+        off_ids = _align(off_offsets + (B + 1) * 8)
+        off_u = _align(off_ids + total * 4)
+        nbytes = _align(off_u + (B * 4 if host_u else 0))
+
+        with self._lock:
+            stg = self._staging_for(device)
+            h = stg.reserve(nbytes)
+            h[off_params:off_params + 6 * B * 4] = params.reshape(-1).view(np.uint8)
+            if use_hist and total:
+                offs = h[off_offsets:off_offsets + (B + 1) * 8].view(np.int64)
+                offs[0] = 0
+                np.cumsum(lens, out=offs[1:])
+                flat = np.fromiter(itertools.chain.from_iterable(all_generated_ids), dtype=np.int64,
+                                   count=total)
+                if flat.min() < -(2 ** 31) or flat.max() >= 2 ** 31:
+                    raise IndexError(_lib.status_string(_lib.NS_ERR_TOKEN_ID_OUT_OF_RANGE))
+                h[off_ids:off_ids + total * 4].view(np.int32)[:] = flat
+            if host_u:
+                hu = uniforms.detach().to(torch.float32).reshape(-1).numpy()
+                if hu.size != B:
+                    raise ValueError("uniforms must have one value per row")
+                h[off_u:off_u + B * 4].view(np.float32)[:] = hu
+            base = stg.upload(nbytes, stream)
+
+            p32 = base + off_params
+            if uniforms is None:
+                u_ptr = 0
+            elif host_u:
+                u_ptr = base + off_u
+            else:
+                ud = uniforms.to(device=device, dtype=torch.float32).reshape(-1).contiguous()
+                if ud.numel() != B:
+                    raise ValueError("uniforms must have one value per row")
+                u_ptr = ud.data_ptr()
+            offset = self.offset
+            self.offset += 1
+            rc = self.lib.ns_sample(
+                logits.data_ptr(), _DTYPES[logits.dtype], B, V, int(logits.stride(0)),
+                (base + off_ids) if (use_hist and total) else None,
+                (base + off_offsets) if (use_hist and total) else None,
+                max_hist,
+                p32, p32 + 4 * B, p32 + 8 * B,
+                p32 + 12 * B, p32 + 16 * B, p32 + 20 * B,
+                u_ptr, self.seed, offset,
+                out.data_ptr(), None, 0, stream.cuda_stream)
+            if u_ptr and not host_u:
+                ud.record_stream(stream)
+        if rc != _lib.NS_OK:
+            raise RuntimeError(f"ns_sample failed: {_lib.status_string(rc)}")
+        return out
+
+    # -------------------------------------------------------------- helpers
+    def _device_for(self, logits: torch.Tensor) -> torch.device:
+        if logits.is_cuda:
+            return logits.device
+        if self.device is not None:
+            return self.device
+        return torch.device("cuda", torch.cuda.current_device())
+
+    def _staging_for(self, device: torch.device) -> _Staging:
+        key = device.index
+        if key not in self._staging:
+            self._staging[key] = _Staging(device)
+        return self._staging[key]
+
+
+class DeviceBatch:
+    """Device-resident per-row inputs (params, history CSR, optional uniforms)
+    for repeated launches on logits that change every step -- the shape of a
+    decode loop whose histories live on the GPU.  ``launch`` is one
+    ``ns_sample`` call with no host work, so it can be captured in a CUDA
+    graph."""
+
+    def __init__(self, histories: Optional[Sequence[Sequence[int]]], params, device,
+                 uniforms: Optional[torch.Tensor] = None, seed: int = 0):
+        self.lib = _lib.load()
+        self.device = torch.device(device)
+        self.batch = len(params)
+        self.params = torch.from_numpy(pack_params(params)).to(self.device)      # [6, B]
+        self.seed = seed
+        B = self.batch
+        if histories is not None and any(len(h) for h in histories):
+            lens = np.array([len(h) for h in histories], dtype=np.int64)
+            offs = np.zeros(B + 1, dtype=np.int64)
+            np.cumsum(lens, out=offs[1:])
+            flat = np.fromiter(itertools.chain.from_iterable(histories), dtype=np.int64, count=int(lens.sum()))
+            self.hist_ids = torch.from_numpy(flat.astype(np.int32)).to(self.device)
+            self.hist_offsets = torch.from_numpy(offs).to(self.device)
+            self.max_history = int(lens.max())
+        else:
+            self.hist_ids = self.hist_offsets = None
+            self.max_history = 0
+        self.uniforms = None if uniforms is None else uniforms.to(self.device, torch.float32).contiguous()
+
+    def nbytes(self) -> int:
+        n = self.params.numel() * 4
+        if self.hist_ids is not None:
+            n += self.hist_ids.numel() * 4 + self.hist_offsets.numel() * 8
+        if self.uniforms is not None:
+            n += self.uniforms.numel() * 4
+        return n
+
+    def launch(self, logits: torch.Tensor, out: torch.Tensor, stream: Optional[torch.cuda.Stream] = None,
+               offset: int = 0) -> int:
+        B, V = logits.shape
+        assert B == self.batch and logits.stride(1) == 1 and out.numel() >= B
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        p = self.params.data_ptr()
+        return self.lib.ns_sample(
+            logits.data_ptr(), _DTYPES[logits.dtype], B, V, int(logits.stride(0)),
+            None if self.hist_ids is None else self.hist_ids.data_ptr(),
+            None if self.hist_offsets is None else self.hist_offsets.data_ptr(),
+            self.max_history, p, p + 4 * B, p + 8 * B, p + 12 * B, p + 16 * B, p + 20 * B,
+            None if self.uniforms is None else self.uniforms.data_ptr(), self.seed, offset,
+            out.data_ptr(), None, 0, s.cuda_stream)

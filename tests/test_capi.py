@@ -1,0 +1,75 @@
+"""C-ABI checks that need no GPU: the library loads, exports every function
+declared in include/*.h, and rejects bad arguments before touching CUDA."""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from b200_sampler import _lib
+from b200_sampler.build import INCLUDE
+
+pytestmark = pytest.mark.skipif(not os.path.exists(_lib.LIB_PATH), reason="library not built")
+
+
+def declared_functions():
+    names = set()
+    for h in glob.glob(os.path.join(INCLUDE, "*.h")):
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"^\s*(?:const\s+)?[a-z_0-9]+\s*\*?\s*(ns_[a-z_0-9]+)\s*\(", src, flags=re.M):
+            names.add(m.group(1))
+    return names
+
+
+def test_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_functions()
+    assert {"ns_sample", "ns_sampler_workspace_bytes", "ns_status_string", "ns_version"} <= names
+    for n in names:
+        assert hasattr(lib, n), n
+    assert set(_lib.PROTOTYPES) >= names
+
+
+def test_status_strings_and_version():
+    lib = _lib.load()
+    assert lib.ns_version() >= 100
+    for code in range(-10, 1):
+        assert lib.ns_status_string(code)
+    assert _lib.status_string(_lib.NS_ERR_INVALID_DISTRIBUTION).startswith("probability tensor")
+
+
+def test_workspace_query():
+    lib = _lib.load()
+    sz = ctypes.c_size_t(123)
+    assert lib.ns_sampler_workspace_bytes(256, 151936, 1024, ctypes.byref(sz)) == 0
+    assert sz.value == 0
+    assert lib.ns_sampler_workspace_bytes(-1, 10, 0, ctypes.byref(sz)) == _lib.NS_ERR_INVALID_ARGUMENT
+
+
+def _call(**kw):
+    lib = _lib.load()
+    a = dict(logits=1, dtype=0, batch=1, vocab=10, row_stride=10, hist_ids=None, hist_offsets=None,
+             max_history=0, temperature=1, top_k=1, top_p=1, rep=None, pres=None, freq=None,
+             uniforms=None, seed=0, offset=0, out=1, ws=None, ws_bytes=0, stream=None)
+    a.update(kw)
+    return lib.ns_sample(*a.values())
+
+
+def test_argument_validation_without_gpu():
+    assert _call(dtype=7) == _lib.NS_ERR_UNSUPPORTED_DTYPE
+    assert _call(vocab=0) == _lib.NS_ERR_INVALID_ARGUMENT
+    assert _call(row_stride=5) == _lib.NS_ERR_INVALID_ARGUMENT
+    assert _call(batch=-1) == _lib.NS_ERR_INVALID_ARGUMENT
+    assert _call(hist_ids=1) == _lib.NS_ERR_INVALID_ARGUMENT        # ids without offsets
+    assert _call(logits=None) == _lib.NS_ERR_INVALID_ARGUMENT
+    assert _call(out=None) == _lib.NS_ERR_INVALID_ARGUMENT
+    assert _call(batch=0, logits=None) == _lib.NS_OK                # empty batch: nothing to do
+
+
+def test_package_has_no_oracle_dependency():
+    pkg = os.path.dirname(_lib.__file__)
+    for f in glob.glob(os.path.join(pkg, "*.py")):
+        src = open(f).read()
+        assert not re.search(r"^\s*(from\s+oracle|import\s+oracle)", src, flags=re.M), f
