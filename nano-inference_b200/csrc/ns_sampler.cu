@@ -1,30 +1,35 @@
 // B200-native token sampler (sm_100a).
 //
 // One launch samples every row of a batch.  Each row is handled by a thread
-// block cluster of C CTAs; CTA r streams columns [r*per_cta, (r+1)*per_cta)
-// of the row once from HBM through a 4-stage bulk-copy (TMA) pipeline into
-// shared memory, and the cluster leader merges the CTAs' results through
+// block cluster of C CTAs (C chosen so rows x C covers the SMs); CTA r owns
+// columns [r*per_cta, (r+1)*per_cta) of the row, and each of its 8 warps owns
+// a contiguous 1/8 of that range.  A warp streams its columns once from HBM
+// through its own 2-stage ring of 4 KB bulk copies (TMA, cp.async.bulk) into
+// shared memory and consumes them with no block-wide barrier: its threshold,
+// candidate buffer and argmax live in warp-uniform registers and warp-private
+// shared memory.  Block and cluster synchronisation happens only at the
+// merge, where the cluster leader combines all warps of all CTAs through
 // distributed shared memory.  Per row, by mode:
 //
 //   GREEDY (temperature == 0; reference sampler.py:60-70)
 //       first-index argmax of the penalised logits (NaN counts as max).
 //   FAST   (0 < top_k <= kFastK; reference sampler.py:73-89, 110-133)
-//       single-pass threshold filter: every CTA keeps, in a shared-memory
-//       candidate buffer, all logits >= a running lower bound of its local
-//       k-th largest value; the bound is raised by an in-shared-memory radix
-//       select whenever the buffer would overflow (the vocabulary is never
-//       sorted).  The leader selects the global k-th value over the union,
-//       then runs top-p and the inverse-CDF draw on the few survivors.
+//       single-pass threshold filter: each warp keeps every logit >= a
+//       running lower bound tau of its local k-th largest value; when its
+//       256-entry buffer fills, a warp-level bitwise radix select raises tau
+//       and compacts (the vocabulary is never sorted).  The leader selects
+//       the global k-th value over the union, then runs top-p and the
+//       inverse-CDF draw on the survivors.
 //   GENERAL (top-k disabled or larger than kFastK): reported as
 //       NS_ERR_UNSUPPORTED by this version.
 //
 // Penalties (reference sampler.py:93-108 plus presence/frequency): before the
-// stream starts, each CTA hashes the row's history ids that fall in its column
-// range (id -> count) and buckets the distinct ids by tile.  When a tile
-// lands in shared memory the bucket's logits are penalised in fp32 (IEEE
-// division / multiplication / subtraction, never contracted into FMAs), kept
-// aside, and their slots overwritten with -inf so the streaming pass sees
-// only un-penalised columns.
+// stream starts, each CTA hashes the row's history ids that fall in its
+// columns (id -> count) and buckets the distinct ids by warp tile.  When a
+// tile lands, its bucket's logits are penalised in fp32 (IEEE division /
+// multiplication / subtraction, never contracted into FMAs), kept aside, and
+// their slots overwritten with -inf so the streaming filter sees only
+// un-penalised columns.
 //
 // Temperature is applied without a per-element division: y = x / T is
 // monotone in x, so the k-th largest y is rn(x_k / T) and the survivors
@@ -51,14 +56,20 @@ namespace ns {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kStages = 4;
-constexpr int kTileBytes = 16384;
-constexpr int kStageStride = kTileBytes + 128;
-constexpr int kCap = 1024;       // per-CTA candidate buffer (entries)
-constexpr int kFastK = 512;      // largest top_k served by the single-pass path
-constexpr int kBins = 256;       // radix digit = 8 bits
-constexpr int kHashMax = 4096;   // distinct history ids per CTA (power of two)
+constexpr int kWTile = 4096;                    // bytes per warp tile
+constexpr int kWStages = 2;                     // per-warp ring depth
+constexpr int kWStageStride = kWTile + 32;      // + alignment lead + vector overrun
+constexpr int kStageBytes = kWarps * kWStages * kWStageStride;
+constexpr int kCapW = 256;                      // per-warp candidate buffer (entries)
+constexpr int kPerLane = kCapW / 32;
+constexpr int kFastK = 128;                     // largest top_k served by the single-pass path
+constexpr int kCandBytes = kWarps * kCapW * 8;  // candidate buffers (x, col)
+constexpr int kBins = 256;                      // radix digit = 8 bits (one bin per thread)
+static_assert(kBins == kThreads, "block_kth_regs clears one bin per thread");
+constexpr int kRefreshTile = 3;                 // FAST: CTA-wide threshold refresh after this warp tile
+constexpr int kHashMax = 8192;                  // distinct history ids per CTA (power of two)
 constexpr int kMaxCluster = 8;
+constexpr int kMaxLists = kMaxCluster * kWarps;
 constexpr unsigned kFull = 0xFFFFFFFFu;
 
 enum : int { MODE_GREEDY = 0, MODE_FAST = 1, MODE_GENERAL = 2 };
@@ -95,24 +106,22 @@ struct Elem<NS_DTYPE_F16> {
 // shared-memory state
 // ---------------------------------------------------------------------------
 struct Misc {
-  int n_cand;      // entries in the candidate buffer
-  int pad2;
-  int flags;       // F_* bits
-  int n_unique;    // distinct history ids in this CTA's range
-  float tau;       // filter threshold (negated domain when T < 0)
-  int r_digit;     // radix-select broadcast
+  int flags;      // F_* bits of this CTA (the leader's becomes the cluster's)
+  int n_unique;   // distinct history ids in this CTA's columns
+  int r_digit;    // radix-select broadcast
   int r_krem;
-  int r_total;
-  int n_merge;     // leader: survivors gathered from the cluster
-  int choose;      // leader: inverse-CDF pick
-  float g_best;    // greedy result of this CTA
-  int g_idx;       // ... as a column of this call's logits
-  int pad0, pad1;
+  int n_merge;    // leader: survivors gathered from the cluster
+  int choose;     // leader: inverse-CDF pick
+  float g_best;   // greedy result of this CTA
+  int g_idx;      // ... as a column of this call's logits
+  int wn[kWarps];  // per-warp candidate counts after streaming
+  float wbest[kWarps];
+  int widx[kWarps];
   double d_red[kWarps];
-  float f_red[kWarps];
   int i_red[kWarps];
-  int roff[kMaxCluster * 2 + 2];
-  int rc0[kMaxCluster * 2 + 2];
+  int roff[kMaxLists + 1];  // leader: union offsets over (rank, warp) lists
+  int rc0[kMaxCluster];     // leader: first column of each rank
+  uint32_t hist[kBins];
 };
 
 struct KArgs {
@@ -123,6 +132,7 @@ struct KArgs {
   int64_t vocab_total;   // global vocabulary size
   const int32_t* hist_ids;
   const int64_t* hist_offsets;
+  int64_t max_history;
   const float* temperature;
   const int32_t* top_k;
   const float* top_p;
@@ -133,29 +143,27 @@ struct KArgs {
   uint64_t seed;
   uint64_t offset;
   int64_t* out_ids;
-  int per_cta;     // columns per CTA, a multiple of the 16-byte vector width
-  int tiles_max;   // tiles per CTA (upper bound)
+  int per_cta;     // columns per CTA (multiple of the 16-byte vector width)
+  int per_warp;    // columns per warp (multiple of the 16-byte vector width)
+  int tpw;         // tiles per warp (upper bound)
   int hash_slots;  // power of two
   int uniq_cap;    // distinct ids the bucket arrays hold
   int merge_cap;   // leader merge area (entries)
-  int64_t max_history;  // host bound on any row's history length
-  uint32_t off_bar, off_cx, off_cid, off_hist, off_hkey, off_hcnt, off_bcol, off_bcnt, off_bx, off_toff,
-      off_tfill, off_misc;
+  uint32_t off_bar, off_cand, off_bcol, off_bcnt, off_bx, off_toff, off_tfill, off_misc;
 };
 
 template <int DT>
 struct Ctx {
   using E = Elem<DT>;
   static constexpr int ES = E::size;
-  static constexpr int VE = 16 / ES;         // elements per 16-byte vector
-  static constexpr int TE = kTileBytes / ES;  // elements per tile
+  static constexpr int VE = 16 / ES;      // elements per 16-byte vector
+  static constexpr int TE = kWTile / ES;  // elements per warp tile
 
   uint8_t* stages;
   uint64_t* bar;
-  float* cx;
-  int* cid;
-  uint32_t* hist;
-  int* hkey;
+  float* cx;  // [kWarps][kCapW]
+  int* cid;   // [kWarps][kCapW]
+  int* hkey;  // aliases the candidate buffers during the prologue
   int* hcnt;
   int* bcol;
   int* bcnt;
@@ -165,22 +173,29 @@ struct Ctx {
   Misc* m;
 
   const uint8_t* rowp;  // column 0 of this row
+  int64_t row;
   int c0, c1;           // this CTA's columns
-  int n_tiles;
+  int pw, tpw;          // per-warp columns / tiles
   int K;
   bool neg;
   float Tabs;
 
-  __device__ __forceinline__ int tile_len(int t) const { return min(TE, c1 - (c0 + t * TE)); }
-  // Elements before the first 16-byte aligned column of the tile, and the
-  // shared-memory slot of the tile's first column (so the aligned body lands
-  // on a 16-byte boundary).
-  __device__ __forceinline__ int tile_head(int t) const {
-    const uintptr_t a = reinterpret_cast<uintptr_t>(rowp) + uintptr_t(c0 + t * TE) * ES;
-    return min(int(((16u - (a & 15u)) & 15u) / ES), tile_len(t));
+  __device__ __forceinline__ int w0(int w) const { return min(c0 + w * pw, c1); }
+  __device__ __forceinline__ int w1(int w) const { return min(c0 + (w + 1) * pw, c1); }
+  __device__ __forceinline__ int wtiles(int w) const { return (w1(w) - w0(w) + TE - 1) / TE; }
+  __device__ __forceinline__ int tile_len(int w, int t) const { return min(TE, w1(w) - (w0(w) + t * TE)); }
+  // Elements before the first 16-byte aligned column of a tile; the tile's
+  // first column goes to shared-memory slot `lead` so the aligned body lands
+  // on a 16-byte boundary.
+  __device__ __forceinline__ int tile_head(int w, int t) const {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(rowp) + uintptr_t(w0(w) + t * TE) * ES;
+    return min(int(((16u - (a & 15u)) & 15u) / ES), tile_len(w, t));
   }
-  __device__ __forceinline__ int tile_lead(int t) const { return (VE - tile_head(t)) % VE; }
-  __device__ __forceinline__ uint8_t* stage(int t) const { return stages + (t % kStages) * kStageStride; }
+  __device__ __forceinline__ int tile_lead(int w, int t) const { return (VE - tile_head(w, t)) % VE; }
+  __device__ __forceinline__ uint8_t* stage(int w, int s) const {
+    return stages + (w * kWStages + s) * kWStageStride;
+  }
+  __device__ __forceinline__ uint64_t* sbar(int w, int s) const { return bar + w * kWStages + s; }
 };
 
 // ---------------------------------------------------------------------------
@@ -219,101 +234,6 @@ __device__ __forceinline__ void unpack16(const uint4& v, float (&x)[Ctx<DT>::VE]
   }
 }
 
-// Reserve n buffer slots without ever exceeding kCap; -1 if they do not fit.
-__device__ __forceinline__ int reserve_slots(Misc* m, int n) {
-  int old = *reinterpret_cast<volatile int*>(&m->n_cand);
-  while (true) {
-    if (old + n > kCap) return -1;
-    const int prev = atomicCAS(&m->n_cand, old, old + n);
-    if (prev == old) return old;
-    old = prev;
-  }
-}
-
-// Warp-aggregated append; all 32 lanes must call it.  Returns true (in every
-// lane) if the warp's entries did not fit; nothing is written then.
-template <int DT>
-__device__ __forceinline__ bool warp_append(const Ctx<DT>& c, bool want, float x, int col) {
-  const unsigned mask = __ballot_sync(kFull, want);
-  if (!mask) return false;
-  const int lane = threadIdx.x & 31;
-  const int leader = __ffs(mask) - 1;
-  int base = 0;
-  if (lane == leader) base = reserve_slots(c.m, __popc(mask));
-  base = __shfl_sync(kFull, base, leader);
-  if (base >= 0 && want) {
-    const int pos = base + __popc(mask & lanemask_lt());
-    c.cx[pos] = x;
-    c.cid[pos] = col;
-  }
-  return base < 0;
-}
-
-// K-th largest (1-based) of the values visited by `for_each` (called by every
-// thread of the CTA with a per-thread share).  Returns false if fewer than K
-// values were visited.  8-bit MSB-first radix select in shared memory.
-template <int DT, class ForEach>
-__device__ bool radix_kth(const Ctx<DT>& c, int K, ForEach for_each, uint32_t* out_key) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  uint32_t prefix = 0, pmask = 0;
-  int krem = K;
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = tid; i < kBins; i += kThreads) c.hist[i] = 0;
-    __syncthreads();
-    for_each([&](float x) {
-      const uint32_t k = f2key(x);
-      if ((k & pmask) == prefix) atomicAdd(&c.hist[(k >> shift) & 0xFFu], 1u);
-    });
-    __syncthreads();
-    if (warp == 0) {
-      uint32_t cnt[8];
-      uint32_t local = 0;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        cnt[q] = c.hist[255 - 8 * lane - q];
-        local += cnt[q];
-      }
-      uint32_t incl = local;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t v = __shfl_up_sync(kFull, incl, o);
-        if (lane >= o) incl += v;
-      }
-      const uint32_t excl = incl - local;
-      const unsigned b = __ballot_sync(kFull, incl >= uint32_t(krem));
-      if (b == 0) {
-        if (lane == 31) {
-          c.m->r_digit = -1;
-          c.m->r_total = int(incl);
-        }
-      } else if (lane == __ffs(b) - 1) {
-        uint32_t cum = excl;
-        int d = 255 - 8 * lane, kr = krem;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          if (cum + cnt[q] >= uint32_t(krem)) {
-            d = 255 - 8 * lane - q;
-            kr = krem - int(cum);
-            break;
-          }
-          cum += cnt[q];
-        }
-        c.m->r_digit = d;
-        c.m->r_krem = kr;
-      }
-    }
-    __syncthreads();
-    const int d = c.m->r_digit;
-    if (d < 0) return false;
-    prefix |= uint32_t(d) << shift;
-    pmask |= 0xFFu << shift;
-    krem = c.m->r_krem;
-    __syncthreads();
-  }
-  *out_key = prefix;
-  return true;
-}
-
 // Smallest x with rn(x / T) >= rn(xk / T) (T > 0): the filter bound that keeps
 // every value whose scaled logit ties the k-th.  Gallop then bisect on keys.
 __device__ float scaled_lower_bound(float xk, float T) {
@@ -345,182 +265,364 @@ __device__ float scaled_lower_bound(float xk, float T) {
   return key2f(hi);
 }
 
-// Keep the buffer entries for which keep(x, col) holds (in place).
-template <int DT, class Keep>
-__device__ void compact_buffer(const Ctx<DT>& c, Keep keep) {
-  constexpr int PER = kCap / kThreads;
-  const int tid = threadIdx.x;
-  const int n = c.m->n_cand;
-  float xs[PER];
-  int cs[PER];
+// ---------------------------------------------------------------------------
+// per-warp candidate buffer (warp-uniform state)
+// ---------------------------------------------------------------------------
+struct WarpCand {
+  float* x;    // this warp's kCapW-entry buffer
+  int* col;
+  float tau;   // filter threshold
+  int n;       // entries in use
+  bool ovf;    // ties exceeded the buffer
+};
+
+// K-th largest key among this warp's buffer entries (n > K): bitwise radix
+// select over registers, one warp reduction per bit.
+__device__ __forceinline__ uint32_t warp_kth_key(const uint32_t (&key)[kPerLane], int K) {
+  uint32_t pre = 0;
+#pragma unroll 1
+  for (int b = 31; b >= 0; --b) {
+    const uint32_t cand = pre | (1u << b);
+    int cnt = 0;
 #pragma unroll
-  for (int q = 0; q < PER; ++q) {
-    const int i = q * kThreads + tid;
-    xs[q] = (i < n) ? c.cx[i] : -INFINITY;
-    cs[q] = (i < n) ? c.cid[i] : 0;
+    for (int q = 0; q < kPerLane; ++q) cnt += (key[q] >= cand) ? 1 : 0;
+    cnt = int(__reduce_add_sync(kFull, unsigned(cnt)));
+    if (cnt >= K) pre = cand;
   }
-  __syncthreads();
-  if (tid == 0) c.m->n_cand = 0;
-  __syncthreads();
+  return pre;
+}
+
+// Raise tau to the collision-safe bound of the warp's K-th largest entry and
+// drop the entries below it.
+template <int DT>
+__device__ void warp_compact(const Ctx<DT>& c, WarpCand& s) {
+  const int lane = threadIdx.x & 31;
+  uint32_t key[kPerLane];
+  int col[kPerLane];
 #pragma unroll
-  for (int q = 0; q < PER; ++q) {
-    const int i = q * kThreads + tid;
-    warp_append(c, (i < n) && keep(xs[q], cs[q]), xs[q], cs[q]);
+  for (int q = 0; q < kPerLane; ++q) {
+    const int i = q * 32 + lane;
+    key[q] = (i < s.n) ? f2key(s.x[i]) : 0u;
+    col[q] = (i < s.n) ? s.col[i] : 0;
   }
-  __syncthreads();
+  __syncwarp();
+  if (s.n > c.K) {
+    const uint32_t kk = warp_kth_key(key, c.K);
+    float t = 0.0f;
+    if (lane == 0) t = scaled_lower_bound(key2f(kk), c.Tabs);
+    s.tau = fmaxf(s.tau, __shfl_sync(kFull, t, 0));
+  }
+  int base = 0;
+#pragma unroll
+  for (int q = 0; q < kPerLane; ++q) {
+    const int i = q * 32 + lane;
+    const float v = key2f(key[q]);
+    const bool keep = (i < s.n) && v >= s.tau;
+    const unsigned mk = __ballot_sync(kFull, keep);
+    if (keep) {
+      const int pos = base + __popc(mk & lanemask_lt());
+      s.x[pos] = v;
+      s.col[pos] = col[q];
+    }
+    base += __popc(mk);
+  }
+  s.n = base;
+  __syncwarp();
+}
+
+// Drop the warp's buffer entries below tau (after tau was raised elsewhere).
+__device__ __forceinline__ void warp_drop_below(WarpCand& s) {
+  const int lane = threadIdx.x & 31;
+  float v[kPerLane];
+  int col[kPerLane];
+#pragma unroll
+  for (int q = 0; q < kPerLane; ++q) {
+    const int i = q * 32 + lane;
+    v[q] = (i < s.n) ? s.x[i] : -INFINITY;
+    col[q] = (i < s.n) ? s.col[i] : 0;
+  }
+  __syncwarp();
+  int base = 0;
+#pragma unroll
+  for (int q = 0; q < kPerLane; ++q) {
+    const bool keep = (q * 32 + lane < s.n) && v[q] >= s.tau;
+    const unsigned mk = __ballot_sync(kFull, keep);
+    if (keep) {
+      const int pos = base + __popc(mk & lanemask_lt());
+      s.x[pos] = v[q];
+      s.col[pos] = col[q];
+    }
+    base += __popc(mk);
+  }
+  s.n = base;
+  __syncwarp();
+}
+
+// Warp-wide append: lane l contributes the elements x[i] whose bit i is set
+// in `bits`, at columns col0 + i.  All 32 lanes call it.  Compacts first when
+// the entries do not fit; a buffer still full afterwards (ties at the
+// threshold) sets s.ovf.
+template <int DT, int N>
+__device__ __forceinline__ void warp_append_bits(const Ctx<DT>& c, WarpCand& s, unsigned bits, const float (&x)[N],
+                                                 int col0) {
+  const int lane = threadIdx.x & 31;
+  int cnt = __popc(bits);
+  int incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(kFull, incl, o);
+    if (lane >= o) incl += v;
+  }
+  int total = __shfl_sync(kFull, incl, 31);
+  if (total == 0) return;
+  if (s.n + total > kCapW) {
+    warp_compact(c, s);
+    unsigned nb = 0;
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+      if (((bits >> i) & 1u) && x[i] >= s.tau) nb |= 1u << i;
+    bits = nb;
+    cnt = __popc(bits);
+    incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += v;
+    }
+    total = __shfl_sync(kFull, incl, 31);
+    if (s.n + total > kCapW) {
+      s.ovf = true;
+      return;
+    }
+  }
+  int pos = s.n + incl - cnt;
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+    if ((bits >> i) & 1u) {
+      s.x[pos] = x[i];
+      s.col[pos] = col0 + i;
+      ++pos;
+    }
+  s.n += total;
 }
 
 // ---------------------------------------------------------------------------
-// producer: one bulk copy per tile (plain loads for an unaligned head / tail)
+// producer: one bulk copy per warp tile (plain loads for an unaligned head /
+// tail); issued by lane 0 of the owning warp
 // ---------------------------------------------------------------------------
 template <int DT>
-__device__ void issue_tile(const Ctx<DT>& c, int t, uint64_t policy) {
+__device__ void issue_tile(const Ctx<DT>& c, int w, int t, uint64_t policy) {
   using E = Elem<DT>;
   constexpr int ES = E::size;
-  const int s = t % kStages;
-  uint8_t* dst = c.stage(t);
-  const int len = c.tile_len(t);
-  const int head = c.tile_head(t);
+  const int s = t % kWStages;
+  const int len = c.tile_len(w, t);
+  const int head = c.tile_head(w, t);
   const int body = (((len - head) * ES) & ~15) / ES;
   const int tail = len - head - body;
-  const int lead = c.tile_lead(t);
-  const typename E::raw* src = reinterpret_cast<const typename E::raw*>(c.rowp) + (c.c0 + t * Ctx<DT>::TE);
-  typename E::raw* d = reinterpret_cast<typename E::raw*>(dst);
+  const int lead = c.tile_lead(w, t);
+  const typename E::raw* src = reinterpret_cast<const typename E::raw*>(c.rowp) + (c.w0(w) + t * Ctx<DT>::TE);
+  typename E::raw* d = reinterpret_cast<typename E::raw*>(c.stage(w, s));
   for (int q = 0; q < head; ++q) d[lead + q] = src[q];
   for (int q = 0; q < tail; ++q) d[lead + head + body + q] = src[head + body + q];
   const uint32_t bytes = uint32_t(body) * ES;
-  mbar_arrive_expect_tx(&c.bar[s], bytes);
-  if (bytes) bulk_g2s(d + lead + head, src + head, bytes, &c.bar[s], policy);
+  mbar_arrive_expect_tx(c.sbar(w, s), bytes);
+  if (bytes) bulk_g2s(d + lead + head, src + head, bytes, c.sbar(w, s), policy);
 }
 
-// ---------------------------------------------------------------------------
-// consumers
-// ---------------------------------------------------------------------------
-// FAST: append every valid value >= tau (tile slots, then the tile's penalised
-// history entries).  NaN or +inf in a sampled row flags F_NAN.  Returns true
-// if any of this thread's warp appends did not fit.
+// Penalise the history columns of warp tile (w, t) in place: the penalised
+// value goes to bx[], the shared-memory slot becomes -inf (in the negated
+// domain when T < 0).  Called by all lanes of the owning warp.
 template <int DT>
-__device__ bool fast_tile(const Ctx<DT>& c, int t, float tau) {
-  bool ovf = false;
-  constexpr int VE = Ctx<DT>::VE, TE = Ctx<DT>::TE;
-  const uint8_t* st = c.stage(t);
-  const int len = c.tile_len(t), lead = c.tile_lead(t);
-  const int n_groups = (lead + len + VE - 1) / VE;
-  const int iters = (n_groups + kThreads - 1) / kThreads;
-  const int colbase = t * TE - lead;
-  for (int it = 0; it < iters; ++it) {
-    const int q = it * kThreads + threadIdx.x;
-    float x[VE];
-    bool hot = false;
-    if (q < n_groups) {
-      const uint4 v = *reinterpret_cast<const uint4*>(st + q * 16);
-      unpack16<DT>(v, x);
-#pragma unroll
-      for (int i = 0; i < VE; ++i) {
-        if (c.neg) x[i] = -x[i];
-        hot |= !(x[i] < tau);
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < VE; ++i) x[i] = -INFINITY;
-    }
-    if (__any_sync(kFull, hot)) {
-#pragma unroll
-      for (int i = 0; i < VE; ++i) {
-        const int e = q * VE + i;
-        const bool valid = (q < n_groups) && e >= lead && e < lead + len;
-        const float xi = x[i];
-        const bool bad = valid && (xi != xi || xi == INFINITY);
-        if (bad) atomicOr(&c.m->flags, F_NAN);
-        ovf |= warp_append(c, valid && !bad && xi >= tau && xi > -INFINITY, xi, colbase + e);
-      }
-    }
+__device__ __forceinline__ void patch_tile(const Ctx<DT>& c, int w, int t, uint8_t* st, float rep, float pres,
+                                           float freq) {
+  using E = Elem<DT>;
+  using R = typename E::raw;
+  const int gt = w * c.tpw + t;
+  const int b0 = c.toff[gt], b1 = c.toff[gt + 1];
+  if (b0 == b1) return;
+  R* sr = reinterpret_cast<R*>(st);
+  const int lead = c.tile_lead(w, t);
+  const int base = w * c.pw + t * Ctx<DT>::TE;  // CTA-relative column of the tile's first element
+  const int lane = threadIdx.x & 31;
+  for (int j = b0 + lane; j < b1; j += 32) {
+    const int e = lead + c.bcol[j] - base;
+    float xp = penalize(E::widen(sr[e]), c.bcnt[j], rep, pres, freq);
+    if (c.neg) xp = -xp;
+    c.bx[j] = xp;
+    sr[e] = c.neg ? E::pinf : E::ninf;
   }
-  const int b0 = c.toff[t], b1 = c.toff[t + 1];
-  const int biters = (b1 - b0 + kThreads - 1) / kThreads;
-  for (int it = 0; it < biters; ++it) {
-    const int j = b0 + it * kThreads + threadIdx.x;
-    const bool in = j < b1;
-    const float xi = in ? c.bx[j] : -INFINITY;
-    const int col = in ? c.bcol[j] : 0;
-    const bool bad = in && (xi != xi || xi == INFINITY);
-    if (bad) atomicOr(&c.m->flags, F_NAN);
-    ovf |= warp_append(c, in && !bad && xi >= tau && xi > -INFINITY, xi, col);
-  }
-  return ovf;
+  fence_proxy_async_smem();
 }
 
-// Values of tile t that the filter would consider at threshold tau.
-template <int DT, class F>
-__device__ __forceinline__ void visit_tile(const Ctx<DT>& c, int t, float tau, F f) {
+// ---------------------------------------------------------------------------
+// per-warp streaming passes
+// ---------------------------------------------------------------------------
+// Load 16-byte group q of a landed tile as fp32 (negated when NEG); groups
+// past the tile read as -inf.
+template <int DT, bool NEG>
+__device__ __forceinline__ void load_group(const uint8_t* st, int q, int n_groups, float (&x)[Ctx<DT>::VE]) {
+  if (q < n_groups) {
+    unpack16<DT>(*reinterpret_cast<const uint4*>(st + q * 16), x);
+    if (NEG) {
+#pragma unroll
+      for (int i = 0; i < Ctx<DT>::VE; ++i) x[i] = -x[i];
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < Ctx<DT>::VE; ++i) x[i] = -INFINITY;
+  }
+}
+
+// Bits of the group's elements that pass the filter (x >= tau); elements
+// outside the tile are masked.  NaN or +inf in a sampled row flags F_NAN.
+template <int DT>
+__device__ __forceinline__ unsigned group_bits(const Ctx<DT>& c, const WarpCand& s, int q,
+                                               const float (&x)[Ctx<DT>::VE], int lead, int len, int n_groups) {
   constexpr int VE = Ctx<DT>::VE;
-  const uint8_t* st = c.stage(t);
-  const int len = c.tile_len(t), lead = c.tile_lead(t);
-  const int n_groups = (lead + len + VE - 1) / VE;
-  for (int q = threadIdx.x; q < n_groups; q += kThreads) {
-    float x[VE];
-    unpack16<DT>(*reinterpret_cast<const uint4*>(st + q * 16), x);
+  unsigned bits = 0, bad = 0;
 #pragma unroll
-    for (int i = 0; i < VE; ++i) {
-      const int e = q * VE + i;
-      const float xi = c.neg ? -x[i] : x[i];
-      if (e >= lead && e < lead + len && xi >= tau && xi > -INFINITY && xi != INFINITY) f(xi);
+  for (int i = 0; i < VE; ++i) {
+    bits |= (x[i] >= s.tau ? 1u : 0u) << i;
+    bad |= (x[i] != x[i] || x[i] == INFINITY) ? 1u : 0u;
+  }
+  const int e0 = q * VE;
+  if (q >= n_groups || e0 < lead || e0 + VE > lead + len) {  // partial group: mask by position
+    unsigned vm = 0;
+#pragma unroll
+    for (int i = 0; i < VE; ++i) vm |= ((q < n_groups && e0 + i >= lead && e0 + i < lead + len) ? 1u : 0u) << i;
+    bits &= vm;
+    if (bad) {
+      bad = 0;
+#pragma unroll
+      for (int i = 0; i < VE; ++i) bad |= (((vm >> i) & 1u) && (x[i] != x[i] || x[i] == INFINITY)) ? 1u : 0u;
     }
   }
-  for (int j = c.toff[t] + threadIdx.x; j < c.toff[t + 1]; j += kThreads) {
-    const float xi = c.bx[j];
-    if (xi >= tau && xi > -INFINITY && xi != INFINITY) f(xi);
+  if (bad) {
+    atomicOr(&c.m->flags, F_NAN);
+#pragma unroll
+    for (int i = 0; i < VE; ++i)
+      if (x[i] != x[i] || x[i] == INFINITY) bits &= ~(1u << i);
   }
+  if (s.tau == -INFINITY) {  // no threshold yet: -inf never becomes a candidate
+#pragma unroll
+    for (int i = 0; i < VE; ++i)
+      if (!(x[i] > -INFINITY)) bits &= ~(1u << i);
+  }
+  return bits;
 }
 
-// Re-process tile t after its appends overflowed the buffer (or directly,
-// while no threshold exists yet): drop the tile's entries, select the K-th
-// largest over buffer + tile, raise tau, compact, append again.
+// Append one hot group per lane: the common case (every lane has at most one
+// passing element) is a ballot; otherwise the general scan.
 template <int DT>
-__device__ void select_tile(const Ctx<DT>& c, int t) {
-  constexpr int TE = Ctx<DT>::TE;
-  const int tid = threadIdx.x;
-  const float tau_old = c.m->tau;
-  const int lo = t * TE, hi = lo + c.tile_len(t);
-  const int n_buf = c.m->n_cand;
-  auto for_each = [&](auto f) {
-    for (int i = tid; i < n_buf; i += kThreads) {
-      const int col = c.cid[i];
-      if (col < lo || col >= hi) f(c.cx[i]);
-    }
-    visit_tile(c, t, tau_old, f);
-  };
-  uint32_t key = 0;
-  const bool have = radix_kth(c, c.K, for_each, &key);
-  if (tid == 0) c.m->tau = have ? fmaxf(tau_old, scaled_lower_bound(key2f(key), c.Tabs)) : tau_old;
-  __syncthreads();
-  const float tau = c.m->tau;
-  compact_buffer(c, [&](float x, int col) { return (col < lo || col >= hi) && x >= tau; });
-  const bool ovf = fast_tile(c, t, tau);
-  if (__syncthreads_or(ovf) && tid == 0) atomicOr(&c.m->flags, F_OVF);
-  __syncthreads();
+__device__ __forceinline__ void group_append(const Ctx<DT>& c, WarpCand& s, int q, const float (&x)[Ctx<DT>::VE],
+                                             bool lane_hot, int lead, int len, int n_groups, int colbase) {
+  constexpr int VE = Ctx<DT>::VE;
+  const unsigned bits = lane_hot ? group_bits(c, s, q, x, lead, len, n_groups) : 0u;
+  if (__any_sync(kFull, (bits & (bits - 1u)) != 0u)) {
+    warp_append_bits(c, s, bits, x, colbase + q * VE);
+    return;
+  }
+  const unsigned mk = __ballot_sync(kFull, bits != 0u);
+  if (!mk) return;
+  if (s.n + __popc(mk) > kCapW) {
+    warp_append_bits(c, s, bits, x, colbase + q * VE);  // compacts
+    return;
+  }
+  if (bits) {
+    const int i = __ffs(bits) - 1;
+    const int pos = s.n + __popc(mk & lanemask_lt());
+    float v = x[0];
+#pragma unroll
+    for (int k = 1; k < VE; ++k)
+      if (i == k) v = x[k];
+    s.x[pos] = v;
+    s.col[pos] = colbase + q * VE + i;
+  }
+  s.n += __popc(mk);
 }
 
-template <int DT>
-__device__ void greedy_tile(const Ctx<DT>& c, int t, float& best, int& bidx) {
+// FAST filter of one landed tile: two 16-byte groups per lane per step, each
+// with its own vote; the common group is a shared load, a compare chain and
+// a vote.
+template <int DT, bool NEG>
+__device__ __forceinline__ void fast_tile(const Ctx<DT>& c, WarpCand& s, int w, int t, const uint8_t* st) {
   constexpr int VE = Ctx<DT>::VE, TE = Ctx<DT>::TE;
-  const uint8_t* st = c.stage(t);
-  const int len = c.tile_len(t), lead = c.tile_lead(t);
+  const int lane = threadIdx.x & 31;
+  const int len = c.tile_len(w, t), lead = c.tile_lead(w, t);
   const int n_groups = (lead + len + VE - 1) / VE;
-  const int colbase = c.c0 + t * TE - lead;
-  for (int q = threadIdx.x; q < n_groups; q += kThreads) {
-    float x[VE];
-    unpack16<DT>(*reinterpret_cast<const uint4*>(st + q * 16), x);
+  const int colbase = w * c.pw + t * TE - lead;  // CTA-relative column of slot 0
+  for (int q0 = 0; q0 < n_groups; q0 += 64) {
+    const int qa = q0 + lane, qb = q0 + 32 + lane;
+    float xa[VE], xb[VE];
+    load_group<DT, NEG>(st, qa, n_groups, xa);
+    load_group<DT, NEG>(st, qb, n_groups, xb);
+    bool ca = true, cb = true;
+#pragma unroll
+    for (int i = 0; i < VE; ++i) {
+      ca = ca && (xa[i] < s.tau);
+      cb = cb && (xb[i] < s.tau);
+    }
+    if (__any_sync(kFull, !ca)) group_append(c, s, qa, xa, !ca, lead, len, n_groups, colbase);
+    if (__any_sync(kFull, !cb)) group_append(c, s, qb, xb, !cb, lead, len, n_groups, colbase);
+  }
+  const int gt = w * c.tpw + t;
+  const int b0 = c.toff[gt], b1 = c.toff[gt + 1];
+  for (int j0 = b0; j0 < b1; j0 += 32) {
+    const int j = j0 + lane;
+    const bool in = j < b1;
+    const float xb1[1] = {in ? c.bx[j] : -INFINITY};
+    const int col = in ? c.bcol[j] : 0;
+    const bool bad = in && (xb1[0] != xb1[0] || xb1[0] == INFINITY);
+    if (bad) atomicOr(&c.m->flags, F_NAN);
+    const bool want = in && !bad && xb1[0] >= s.tau && xb1[0] > -INFINITY;
+    warp_append_bits(c, s, want ? 1u : 0u, xb1, col);
+  }
+}
+
+// GREEDY of one landed tile: per-lane running first-index argmax.  A lane sees
+// its slots in increasing column order, so a strict '>' keeps the first
+// index; a NaN-propagating group max skips groups that cannot win.  Bucket
+// entries arrive out of order and use the full comparison.
+template <int DT>
+__device__ __forceinline__ void greedy_group(const float (&x)[Ctx<DT>::VE], int q, int lead, int len, int n_groups,
+                                             int colbase, float& best, int& bidx) {
+  constexpr int VE = Ctx<DT>::VE;
+  float m = x[0];
+#pragma unroll
+  for (int i = 1; i < VE; ++i) m = fmax_nan(m, x[i]);
+  if (!(m <= best) || bidx == INT_MAX) {
 #pragma unroll
     for (int i = 0; i < VE; ++i) {
       const int e = q * VE + i;
-      if (e >= lead && e < lead + len && better(x[i], colbase + e, best, bidx)) {
+      const bool valid = (q < n_groups) && e >= lead && e < lead + len;
+      if (valid && (bidx == INT_MAX || x[i] > best || (x[i] != x[i] && best == best))) {
         best = x[i];
         bidx = colbase + e;
       }
     }
   }
-  for (int j = c.toff[t] + threadIdx.x; j < c.toff[t + 1]; j += kThreads) {
+}
+
+template <int DT>
+__device__ __forceinline__ void greedy_tile(const Ctx<DT>& c, int w, int t, const uint8_t* st, float& best,
+                                            int& bidx) {
+  constexpr int VE = Ctx<DT>::VE, TE = Ctx<DT>::TE;
+  const int lane = threadIdx.x & 31;
+  const int len = c.tile_len(w, t), lead = c.tile_lead(w, t);
+  const int n_groups = (lead + len + VE - 1) / VE;
+  const int colbase = c.c0 + w * c.pw + t * TE - lead;  // call-local column of slot 0
+  if (best == best) {  // a lane that has seen a NaN keeps its first NaN
+    for (int q0 = 0; q0 < n_groups; q0 += 64) {
+      const int qa = q0 + lane, qb = q0 + 32 + lane;
+      float xa[VE], xb[VE];
+      load_group<DT, false>(st, qa, n_groups, xa);
+      load_group<DT, false>(st, qb, n_groups, xb);
+      greedy_group<DT>(xa, qa, lead, len, n_groups, colbase, best, bidx);
+      greedy_group<DT>(xb, qb, lead, len, n_groups, colbase, best, bidx);
+    }
+  }
+  const int gt = w * c.tpw + t;
+  for (int j = c.toff[gt] + lane; j < c.toff[gt + 1]; j += 32) {
     const int col = c.c0 + c.bcol[j];
     if (better(c.bx[j], col, best, bidx)) {
       best = c.bx[j];
@@ -529,13 +631,52 @@ __device__ void greedy_tile(const Ctx<DT>& c, int t, float& best, int& bidx) {
   }
 }
 
+// Stream tiles [t_begin, t_end) of this warp's columns (its first kWStages
+// copies were issued before the history prologue; tiles below n_ready were
+// already waited for and patched).  mode: GREEDY or FAST.  Returns false if a
+// bounded wait gave up (F_TIMEOUT is set); in-flight copies are drained first.
+template <int DT>
+__device__ __forceinline__ bool stream_warp(const Ctx<DT>& c, int mode, uint64_t policy, float rep, float pres, float freq,
+                            int t_begin, int t_end, int n_ready, WarpCand& s, float& best, int& bidx) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nt = c.wtiles(w);
+  for (int t = t_begin; t < min(nt, t_end); ++t) {
+    const int sidx = t % kWStages;
+    uint8_t* st = c.stage(w, sidx);
+    if (t >= n_ready) {
+      const bool ok = mbar_wait_bounded(c.sbar(w, sidx), uint32_t(t / kWStages) & 1u);
+      if (!__all_sync(kFull, ok)) {
+        if (lane == 0) {
+          atomicOr(&c.m->flags, F_TIMEOUT);
+          for (int u = t; u < min(nt, t + kWStages); ++u)
+            mbar_wait_bounded(c.sbar(w, u % kWStages), uint32_t(u / kWStages) & 1u);
+        }
+        __syncwarp();
+        return false;
+      }
+      patch_tile(c, w, t, st, rep, pres, freq);
+      __syncwarp();
+    }
+    if (mode == MODE_GREEDY) {
+      greedy_tile(c, w, t, st, best, bidx);
+    } else if (!s.ovf) {
+      if (c.neg)
+        fast_tile<DT, true>(c, s, w, t, st);
+      else
+        fast_tile<DT, false>(c, s, w, t, st);
+    }
+    __syncwarp();
+    if (lane == 0 && t + kWStages < nt) issue_tile(c, w, t + kWStages, policy);
+  }
+  return true;
+}
+
 __device__ __forceinline__ void hash_insert(int* hkey, int* hcnt, Misc* m, int key, int slots) {
   uint32_t h = (uint32_t(key) * 2654435761u) & uint32_t(slots - 1);
   for (int probe = 0; probe < slots; ++probe) {
     const int prev = atomicCAS(&hkey[h], -1, key);
     if (prev == -1) {
       atomicAdd(&hcnt[h], 1);
-      atomicAdd(&m->n_unique, 1);
       return;
     }
     if (prev == key) {
@@ -548,8 +689,70 @@ __device__ __forceinline__ void hash_insert(int* hkey, int* hcnt, Misc* m, int k
 }
 
 // ---------------------------------------------------------------------------
-// block-level helpers for the leader
+// block-level helpers for the cluster leader
 // ---------------------------------------------------------------------------
+// K-th largest (1-based) of the values visited by `for_each` (called by every
+// thread with a per-thread share).  False if fewer than K values were visited.
+// 8-bit MSB-first radix select with shared-memory histograms.
+template <class ForEach>
+__device__ bool block_radix_kth(Misc* m, int K, ForEach for_each, uint32_t* out_key) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint32_t prefix = 0, pmask = 0;
+  int krem = K;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = tid; i < kBins; i += kThreads) m->hist[i] = 0;
+    __syncthreads();
+    for_each([&](float x) {
+      const uint32_t k = f2key(x);
+      if ((k & pmask) == prefix) atomicAdd(&m->hist[(k >> shift) & 0xFFu], 1u);
+    });
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t cnt[8];
+      uint32_t local = 0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        cnt[q] = m->hist[255 - 8 * lane - q];
+        local += cnt[q];
+      }
+      uint32_t incl = local;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t v = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const uint32_t excl = incl - local;
+      const unsigned b = __ballot_sync(kFull, incl >= uint32_t(krem));
+      if (b == 0) {
+        if (lane == 0) m->r_digit = -1;
+      } else if (lane == __ffs(b) - 1) {
+        uint32_t cum = excl;
+        int d = 255 - 8 * lane, kr = krem;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (cum + cnt[q] >= uint32_t(krem)) {
+            d = 255 - 8 * lane - q;
+            kr = krem - int(cum);
+            break;
+          }
+          cum += cnt[q];
+        }
+        m->r_digit = d;
+        m->r_krem = kr;
+      }
+    }
+    __syncthreads();
+    const int d = m->r_digit;
+    if (d < 0) return false;
+    prefix |= uint32_t(d) << shift;
+    pmask |= 0xFFu << shift;
+    krem = m->r_krem;
+    __syncthreads();
+  }
+  *out_key = prefix;
+  return true;
+}
+
 __device__ void bitonic_sort_u64(uint64_t* s, int n, bool desc) {
   for (int k = 2; k <= n; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
@@ -622,6 +825,113 @@ __device__ __forceinline__ int status_from_flags(int f, bool greedy) {
   return NS_OK;
 }
 
+constexpr int kSmallN = 128;
+
+// Leader, FAST rows with n <= kSmallN survivors: sort by rank counting (thread
+// i owns survivor i), then one warp computes the softmax prefix sums with
+// shuffles (4 positions per lane).
+template <int DT>
+__device__ void finalize_small(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, int n) {
+  Misc* m = c.m;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float* my = reinterpret_cast<const float*>(c.stages);
+  const int* mid = reinterpret_cast<const int*>(c.stages + size_t(a.merge_cap) * 4);
+  float* sy = reinterpret_cast<float*>(c.stages + size_t(a.merge_cap) * 8);
+  int* sid = reinterpret_cast<int*>(sy + kSmallN);
+  float* se = reinterpret_cast<float*>(sid + kSmallN);
+  int* kid = reinterpret_cast<int*>(se + kSmallN);
+  float* kw = reinterpret_cast<float*>(kid + kSmallN);
+  if (tid < n) {  // position in (y desc, id asc) order
+    const float yi = my[tid] + 0.0f;
+    const int ii = mid[tid];
+    int rank = 0;
+    for (int j = 0; j < n; ++j) {
+      const float yj = my[j] + 0.0f;
+      rank += (yj > yi || (yj == yi && mid[j] < ii)) ? 1 : 0;
+    }
+    sy[rank] = yi;
+    sid[rank] = ii;
+  }
+  __syncthreads();
+  const float M = sy[0];
+  if (!(M < INFINITY)) {
+    if (tid == 0) a.out_ids[row] = NS_ERR_INVALID_DISTRIBUTION;
+    return;
+  }
+  if (warp == 0) {
+    // softmax weights and the top-p cut: sorted position j+1 survives iff
+    // cumsum[j] <= p (reference sampler.py:127-131)
+    double e[4], local = 0.0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int j = lane * 4 + k;
+      const float w = (j < n) ? expf(__fsub_rn(sy[j], M)) : 0.0f;
+      if (j < n) se[j] = w;
+      e[k] = double(w);
+      local += e[k];
+    }
+    double incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double v = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const double total = __shfl_sync(kFull, incl, 31);
+    int L = n;
+    if (topp > 0.0f && topp < 1.0f) {
+      int cnt = 0;
+      double run = incl - local;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int j = lane * 4 + k;
+        run += e[k];
+        cnt += (j <= n - 2 && run <= double(topp) * total) ? 1 : 0;
+      }
+      L = 1 + int(__reduce_add_sync(kFull, unsigned(cnt)));
+    }
+    if (lane == 0) m->r_krem = L;
+  }
+  __syncthreads();
+  const int L = m->r_krem;
+  if (tid < L) {  // ascending-id order among the kept positions
+    const int ii = sid[tid];
+    int r2 = 0;
+    for (int j = 0; j < L; ++j) r2 += (sid[j] < ii) ? 1 : 0;
+    kid[r2] = ii;
+    kw[r2] = se[tid];
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // inverse CDF: the first kept id whose running weight exceeds u * total
+    const float u = a.uniforms ? a.uniforms[row] : philox_uniform(a.seed, a.offset, uint64_t(row));
+    double e[4], local = 0.0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int j = lane * 4 + k;
+      e[k] = (j < L) ? double(kw[j]) : 0.0;
+      local += e[k];
+    }
+    double incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double v = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const double total = __shfl_sync(kFull, incl, 31);
+    const double target = double(u) * total;
+    int first = INT_MAX;
+    double run = incl - local;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int j = lane * 4 + k;
+      run += e[k];
+      if (first == INT_MAX && j < L && run > target) first = j;
+    }
+    first = int(__reduce_min_sync(kFull, unsigned(first)));
+    if (lane == 0) a.out_ids[row] = int64_t(kid[first == INT_MAX ? L - 1 : first]) + a.vocab_offset;
+  }
+}
+
 // Leader, FAST rows: survivors sorted by (y desc, id asc); softmax; top-p cut
 // (keep sorted j iff j == 0 or cumsum[j-1] <= p, reference sampler.py:122-131);
 // then the inverse-CDF draw over the kept ids in ascending id order.
@@ -635,6 +945,10 @@ __device__ void finalize_row(const Ctx<DT>& c, const KArgs& a, int64_t row, floa
   uint64_t* keys = reinterpret_cast<uint64_t*>(c.stages + size_t(a.merge_cap) * 8);
   if (n == 0) {
     if (tid == 0) a.out_ids[row] = NS_ERR_INVALID_DISTRIBUTION;
+    return;
+  }
+  if (n <= kSmallN) {
+    finalize_small(c, a, row, topp, n);
     return;
   }
   int n2 = 1;
@@ -688,6 +1002,160 @@ __device__ void finalize_row(const Ctx<DT>& c, const KArgs& a, int64_t row, floa
   }
 }
 
+// K-th largest (1-based) of the non-zero keys held in registers by all
+// threads of the block (zero = empty slot).  8-bit MSB-first radix select
+// with one shared-memory histogram per round (12 block barriers).  Returns
+// false if fewer than K keys are present.
+template <int R>
+__device__ __forceinline__ bool block_kth_regs(Misc* m, const uint32_t (&key)[R], int K, uint32_t* out_key) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint32_t prefix = 0, pmask = 0;
+  int krem = K;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    m->hist[tid] = 0;  // kBins == kThreads
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < R; ++q)
+      if (key[q] != 0u && (key[q] & pmask) == prefix) atomicAdd(&m->hist[(key[q] >> shift) & 0xFFu], 1u);
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t cnt[8];
+      uint32_t local = 0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        cnt[q] = m->hist[255 - 8 * lane - q];
+        local += cnt[q];
+      }
+      uint32_t incl = local;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t v = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const uint32_t excl = incl - local;
+      const unsigned b = __ballot_sync(kFull, incl >= uint32_t(krem));
+      if (b == 0) {
+        if (lane == 0) m->r_digit = -1;
+      } else if (lane == __ffs(b) - 1) {
+        uint32_t cum = excl;
+        int d = 255 - 8 * lane, kr = krem;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (cum + cnt[q] >= uint32_t(krem)) {
+            d = 255 - 8 * lane - q;
+            kr = krem - int(cum);
+            break;
+          }
+          cum += cnt[q];
+        }
+        m->r_digit = d;
+        m->r_krem = kr;
+      }
+    }
+    __syncthreads();
+    const int d = m->r_digit;
+    if (d < 0) return false;
+    prefix |= uint32_t(d) << shift;
+    pmask |= 0xFFu << shift;
+    krem = m->r_krem;
+  }
+  *out_key = prefix;
+  return true;
+}
+
+// Leader, FAST rows: the K-th largest value over the union of every warp list
+// of every CTA in the cluster (read through distributed shared memory), then
+// the survivors rn(x / T) >= rn(x_K / T) into the merge area.  Up to
+// kThreads * kMergeReg entries are held in registers and selected bit by bit
+// (one block count per bit); larger unions use the shared-memory radix select.
+constexpr int kMergeReg = 16;
+
+template <int DT>
+__device__ __forceinline__ void leader_gather(const Ctx<DT>& c, const KArgs& a, cg::cluster_group& cluster, int CL) {
+  Misc* m = c.m;
+  const int tid = threadIdx.x;
+  const int nl = CL * kWarps;
+  const int tot = m->roff[nl];
+  auto owner = [&](int gi) {
+    int lo = 0, hi = nl - 1;  // last list l with roff[l] <= gi
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (m->roff[mid] <= gi)
+        lo = mid;
+      else
+        hi = mid - 1;
+    }
+    return lo;
+  };
+  float* my = reinterpret_cast<float*>(c.stages);
+  int* mid = reinterpret_cast<int*>(c.stages + size_t(a.merge_cap) * 4);
+  if (tot <= kThreads * kMergeReg) {
+    uint32_t key[kMergeReg];
+    int col[kMergeReg];
+#pragma unroll
+    for (int q = 0; q < kMergeReg; ++q) {
+      const int gi = q * kThreads + tid;
+      key[q] = 0u;
+      col[q] = 0;
+      if (gi < tot) {
+        const int l = owner(gi);
+        const int r = l / kWarps, idx = (l % kWarps) * kCapW + gi - m->roff[l];
+        key[q] = f2key(cluster.map_shared_rank(c.cx, r)[idx]);
+        col[q] = cluster.map_shared_rank(c.cid, r)[idx] + m->rc0[r];
+      }
+    }
+    float thr = -INFINITY;
+    uint32_t kk = 0;
+    if (tot > c.K && block_kth_regs(m, key, c.K, &kk)) thr = __fdiv_rn(key2f(kk), c.Tabs);
+#pragma unroll
+    for (int q = 0; q < kMergeReg; ++q) {
+      if (key[q] == 0u) continue;
+      const float y = __fdiv_rn(key2f(key[q]), c.Tabs);
+      if (y >= thr) {
+        const int pos = atomicAdd(&m->n_merge, 1);
+        if (pos < a.merge_cap) {
+          my[pos] = y;
+          mid[pos] = col[q];
+        }
+      }
+    }
+  } else {
+    uint32_t key = 0;
+    const bool have = (tot > c.K) && block_radix_kth(
+                                         m, c.K,
+                                         [&](auto f) {
+                                           for (int gi = tid; gi < tot; gi += kThreads) {
+                                             const int l = owner(gi);
+                                             const float* rcx =
+                                                 cluster.map_shared_rank(c.cx, l / kWarps) + (l % kWarps) * kCapW;
+                                             f(rcx[gi - m->roff[l]]);
+                                           }
+                                         },
+                                         &key);
+    const float thr = have ? __fdiv_rn(key2f(key), c.Tabs) : -INFINITY;
+    for (int gi = tid; gi < tot; gi += kThreads) {
+      const int l = owner(gi);
+      const int r = l / kWarps, wl = l % kWarps;
+      const float* rcx = cluster.map_shared_rank(c.cx, r) + wl * kCapW;
+      const int* rcid = cluster.map_shared_rank(c.cid, r) + wl * kCapW;
+      const float y = __fdiv_rn(rcx[gi - m->roff[l]], c.Tabs);
+      if (y >= thr) {
+        const int pos = atomicAdd(&m->n_merge, 1);
+        if (pos < a.merge_cap) {
+          my[pos] = y;
+          mid[pos] = rcid[gi - m->roff[l]] + m->rc0[r];
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0 && m->n_merge > a.merge_cap) {
+    m->flags |= F_OVF;
+    a.out_ids[c.row] = NS_ERR_CANDIDATE_OVERFLOW;
+  }
+  __syncthreads();
+}
+
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
@@ -705,11 +1173,10 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
   C_ c;
   c.stages = smem;
   c.bar = reinterpret_cast<uint64_t*>(smem + a.off_bar);
-  c.cx = reinterpret_cast<float*>(smem + a.off_cx);
-  c.cid = reinterpret_cast<int*>(smem + a.off_cid);
-  c.hist = reinterpret_cast<uint32_t*>(smem + a.off_hist);
-  c.hkey = reinterpret_cast<int*>(smem + a.off_hkey);
-  c.hcnt = reinterpret_cast<int*>(smem + a.off_hcnt);
+  c.cx = reinterpret_cast<float*>(smem + a.off_cand);
+  c.cid = reinterpret_cast<int*>(smem + a.off_cand + kWarps * kCapW * 4);
+  c.hkey = reinterpret_cast<int*>(smem + a.off_cand);
+  c.hcnt = reinterpret_cast<int*>(smem + a.off_cand + size_t(a.hash_slots) * 4);
   c.bcol = reinterpret_cast<int*>(smem + a.off_bcol);
   c.bcnt = reinterpret_cast<int*>(smem + a.off_bcnt);
   c.bx = reinterpret_cast<float*>(smem + a.off_bx);
@@ -739,196 +1206,219 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     h0 = a.hist_offsets[row];
     h1 = a.hist_offsets[row + 1];
   }
-  const bool pen = (h1 > h0) && (rep != 1.0f || pres != 0.0f || freq != 0.0f);
+  const bool pen = (h1 > h0) && (rep != 1.0f || pres != 0.0f || freq != 0.0f) && mode != MODE_GENERAL;
   c.rowp = reinterpret_cast<const uint8_t*>(a.logits) + size_t(row) * size_t(a.row_stride) * C_::ES;
+  c.row = row;
   c.c0 = int(min(int64_t(rank) * a.per_cta, a.vocab));
   c.c1 = int(min(int64_t(c.c0) + a.per_cta, a.vocab));
-  int n_tiles = (c.c1 - c.c0 + TE - 1) / TE;
-  if (mode == MODE_GENERAL) n_tiles = 0;
-  c.n_tiles = n_tiles;
+  c.pw = a.per_warp;
+  c.tpw = a.tpw;
+  const int n_tiles_all = kWarps * a.tpw;
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(&c.bar[s], 1);
+    for (int s = 0; s < kWarps * kWStages; ++s) mbar_init(&c.bar[s], 1);
     fence_mbar_init();
-    m->n_cand = 0;
     m->flags = (mode == MODE_GENERAL) ? F_UNSUP : 0;
     m->n_unique = 0;
-    m->tau = -INFINITY;
     m->n_merge = 0;
     m->choose = INT_MAX;
     m->g_best = -INFINITY;
     m->g_idx = INT_MAX;
   }
-  for (int i = tid; i < a.hash_slots; i += kThreads) {
-    c.hkey[i] = -1;
-    c.hcnt[i] = 0;
-  }
-  for (int i = tid; i <= a.tiles_max; i += kThreads) {
+  if (pen)
+    for (int i = tid; i < a.hash_slots; i += kThreads) {
+      c.hkey[i] = -1;
+      c.hcnt[i] = 0;
+    }
+  for (int i = tid; i <= n_tiles_all; i += kThreads) {
     c.toff[i] = 0;
     c.tfill[i] = 0;
   }
   __syncthreads();
 
   const uint64_t policy = l2_policy_evict_first();
-  int issued = 0;  // meaningful in thread 0 only
-  if (tid == 0) {
-    issued = min(kStages, n_tiles);
-    for (int t = 0; t < issued; ++t) issue_tile(c, t, policy);
+  const bool streams = (mode != MODE_GENERAL);
+  // each warp starts its first copies now so they overlap the history prologue
+  if (streams && lane == 0) {
+    const int nt = c.wtiles(warp);
+    for (int t = 0; t < min(kWStages, nt); ++t) issue_tile(c, warp, t, policy);
   }
 
-  // ---- history: distinct in-range ids with counts, bucketed by tile ----
-  if (pen && mode != MODE_GENERAL) {
-    for (int64_t i = h0 + tid; i < h1; i += kThreads) {
-      const int id = a.hist_ids[i];
-      if (id < 0 || int64_t(id) >= a.vocab_total) {
-        atomicOr(&m->flags, F_BADID);
-        continue;
+  // ---- history: distinct in-range ids with counts, bucketed by warp tile ----
+  if (pen) {
+    constexpr int kHB = 8;  // ids loaded per thread before inserting (one round trip per batch)
+    for (int64_t base = h0; base < h1; base += int64_t(kThreads) * kHB) {
+      int ids[kHB];
+#pragma unroll
+      for (int q = 0; q < kHB; ++q) {
+        const int64_t i = base + int64_t(q) * kThreads + tid;
+        ids[q] = (i < h1) ? a.hist_ids[i] : INT_MIN;
       }
-      const int64_t lc = int64_t(id) - a.vocab_offset;
-      if (lc >= c.c0 && lc < c.c1) hash_insert(c.hkey, c.hcnt, m, int(lc - c.c0), a.hash_slots);
+#pragma unroll
+      for (int q = 0; q < kHB; ++q) {
+        const int id = ids[q];
+        if (id == INT_MIN) continue;
+        if (id < 0 || int64_t(id) >= a.vocab_total) {
+          atomicOr(&m->flags, F_BADID);
+          continue;
+        }
+        const int64_t lc = int64_t(id) - a.vocab_offset;
+        if (lc >= c.c0 && lc < c.c1) hash_insert(c.hkey, c.hcnt, m, int(lc - c.c0), a.hash_slots);
+      }
     }
     __syncthreads();
-    if (m->n_unique > a.uniq_cap) {
+    int occupied = 0;
+    for (int i = tid; i < a.hash_slots; i += kThreads) occupied += (c.hkey[i] >= 0) ? 1 : 0;
+    const int nu = block_sum_int(m, occupied);
+    if (nu > a.uniq_cap) {
       if (tid == 0) atomicOr(&m->flags, F_HIST);
-    } else if (m->n_unique > 0) {
+    } else if (nu > 0) {
+      auto tile_of = [&](int key) {
+        const int w = key / c.pw;
+        return w * c.tpw + (key - w * c.pw) / TE;
+      };
       for (int i = tid; i < a.hash_slots; i += kThreads)
-        if (c.hkey[i] >= 0) atomicAdd(&c.tfill[c.hkey[i] / TE], 1);
+        if (c.hkey[i] >= 0) atomicAdd(&c.tfill[tile_of(c.hkey[i])], 1);
       __syncthreads();
       if (warp == 0) {
         int carry = 0;
-        for (int base = 0; base < n_tiles; base += 32) {
+        for (int base = 0; base < n_tiles_all; base += 32) {
           const int t = base + lane;
-          const int v = (t < n_tiles) ? c.tfill[t] : 0;
+          const int v = (t < n_tiles_all) ? c.tfill[t] : 0;
           int incl = v;
 #pragma unroll
           for (int o = 1; o < 32; o <<= 1) {
             const int w = __shfl_up_sync(kFull, incl, o);
             if (lane >= o) incl += w;
           }
-          if (t < n_tiles) {
+          if (t < n_tiles_all) {
             c.toff[t] = carry + incl - v;
             c.tfill[t] = 0;
           }
           carry += __shfl_sync(kFull, incl, 31);
         }
-        if (lane == 0) c.toff[n_tiles] = carry;
+        if (lane == 0) c.toff[n_tiles_all] = carry;
       }
       __syncthreads();
       for (int i = tid; i < a.hash_slots; i += kThreads) {
         const int key = c.hkey[i];
         if (key >= 0) {
-          const int t = key / TE;
+          const int t = tile_of(key);
           const int pos = c.toff[t] + atomicAdd(&c.tfill[t], 1);
           c.bcol[pos] = key;
           c.bcnt[pos] = c.hcnt[i];
         }
       }
     }
-    __syncthreads();
+    __syncthreads();  // the hash is dead from here on: its memory holds the candidate buffers
   }
 
-  // ---- stream the row ----
-  // Per-tile decisions that depend on other warps (a timed-out wait, an
-  // overflowing append) are combined with __syncthreads_or so every thread of
-  // the CTA takes the same branch.
-  float g_best = -INFINITY;
-  int g_idx = INT_MAX;
-  int t_done = 0;
-  bool ovf_local = false;  // this thread's warp overflowed while appending tile t-1
-  bool timed_out = false;
-  for (int t = 0; t < n_tiles; ++t) {
-    const bool ok = mbar_wait_bounded(&c.bar[t % kStages], uint32_t(t / kStages) & 1u);
-    if (ok) {
-      uint8_t* st = c.stage(t);
-      using R = typename Elem<DT>::raw;
-      R* sr = reinterpret_cast<R*>(st);
-      const int lead = c.tile_lead(t);
-      for (int j = c.toff[t] + tid; j < c.toff[t + 1]; j += kThreads) {
-        const int e = lead + c.bcol[j] - t * TE;
-        float xp = penalize(Elem<DT>::widen(sr[e]), c.bcnt[j], rep, pres, freq);
-        if (c.neg) xp = -xp;
-        c.bx[j] = xp;
-        sr[e] = c.neg ? Elem<DT>::pinf : Elem<DT>::ninf;
+  // ---- stream: every warp independently ----
+  WarpCand s;
+  s.x = c.cx + warp * kCapW;
+  s.col = c.cid + warp * kCapW;
+  s.tau = -INFINITY;
+  s.n = 0;
+  s.ovf = false;
+  float best = -INFINITY;
+  int bidx = INT_MAX;
+  int n_ready = 0;
+  if (mode == MODE_FAST) {
+    // Seed tau from a CTA-wide sample: the K-th largest of the 256 per-thread
+    // maxima over every warp's first kWStages tiles.  They are distinct
+    // elements of this CTA's columns, so their K-th largest is a lower bound
+    // of the CTA's K-th largest, and for K << 256 it is nearly as tight as
+    // the sample's own.
+    float tmax = -INFINITY;
+    const int nr = min(kWStages, c.wtiles(warp));
+    bool ready = true;
+    for (int t = 0; t < nr; ++t) ready = ready && __all_sync(kFull, mbar_wait_bounded(c.sbar(warp, t), 0u));
+    if (ready) {
+      n_ready = nr;
+      constexpr int VE = C_::VE;
+      for (int t = 0; t < nr; ++t) {
+        uint8_t* st = c.stage(warp, t);
+        patch_tile(c, warp, t, st, rep, pres, freq);
+        __syncwarp();
+        const int len = c.tile_len(warp, t), lead = c.tile_lead(warp, t);
+        const int n_groups = (lead + len + VE - 1) / VE;
+        for (int q = lane; q < n_groups; q += 32) {
+          float x[VE];
+          unpack16<DT>(*reinterpret_cast<const uint4*>(st + q * 16), x);
+#pragma unroll
+          for (int i = 0; i < VE; ++i) {
+            const int e = q * VE + i;
+            const float xk = c.neg ? -x[i] : x[i];
+            if (e >= lead && e < lead + len && xk > -INFINITY && xk < INFINITY) tmax = fmaxf(tmax, xk);
+          }
+        }
+        const int gt = warp * c.tpw + t;
+        for (int j = c.toff[gt] + lane; j < c.toff[gt + 1]; j += 32) {
+          const float xk = c.bx[j];
+          if (xk > -INFINITY && xk < INFINITY) tmax = fmaxf(tmax, xk);
+        }
       }
-      fence_proxy_async_smem();
     }
-    bool prev_ovf = false;
-    if (__syncthreads_or(!ok || ovf_local)) {
-      if (__syncthreads_or(!ok)) {
-        if (tid == 0) atomicOr(&m->flags, F_TIMEOUT);
-        timed_out = true;
-        break;
+    const uint32_t mk = (tmax > -INFINITY) ? f2key(tmax) : 0u;
+    if (__syncthreads_count(mk != 0u) >= c.K) {
+      uint32_t pre = 0;
+      for (int b = 31; b >= 0; --b) {
+        const uint32_t cand = pre | (1u << b);
+        if (__syncthreads_count(mk >= cand) >= c.K) pre = cand;
       }
-      prev_ovf = __syncthreads_or(ovf_local);
-    }
-    ovf_local = false;
-    t_done = t + 1;
-    if (mode == MODE_FAST && prev_ovf && !(m->flags & F_OVF)) select_tile(c, t - 1);
-    if (tid == 0 && t > 0 && issued < n_tiles) {
-      issue_tile(c, issued, policy);
-      ++issued;
-    }
-    if (mode == MODE_GREEDY) {
-      greedy_tile(c, t, g_best, g_idx);
-    } else if (!(m->flags & F_OVF)) {
-      const float tau = m->tau;
-      if (tau == -INFINITY && c.tile_len(t) + (c.toff[t + 1] - c.toff[t]) > kCap / 2)
-        select_tile(c, t);
-      else
-        ovf_local = fast_tile(c, t, tau);
+      s.tau = scaled_lower_bound(key2f(pre), c.Tabs);
     }
   }
-  const bool last_ovf = __syncthreads_or(ovf_local);
-  // After a timeout, wait (bounded) for copies still in flight before the
-  // shared memory is reused or released.
-  if (tid == 0) {
-    for (int t = t_done; t < issued; ++t) mbar_wait_bounded(&c.bar[t % kStages], uint32_t(t / kStages) & 1u);
-  }
-  __syncthreads();
-
-  if (mode == MODE_FAST && !timed_out && !(m->flags & F_OVF)) {
-    if (last_ovf) select_tile(c, n_tiles - 1);
-    if (!(m->flags & F_OVF) && m->n_cand > c.K) {
-      const int n = m->n_cand;
-      uint32_t key = 0;
-      const bool have = radix_kth(
-          c, c.K,
-          [&](auto f) {
-            for (int i = tid; i < n; i += kThreads) f(c.cx[i]);
-          },
-          &key);
-      if (tid == 0 && have) m->tau = fmaxf(m->tau, scaled_lower_bound(key2f(key), c.Tabs));
-      __syncthreads();
-      const float tau = m->tau;
-      compact_buffer(c, [&](float x, int) { return x >= tau; });
+  bool ok = true;
+  if (streams) {
+    if (mode == MODE_FAST && c.tpw >= 2 * (kRefreshTile + 1)) {
+      ok = stream_warp(c, mode, policy, rep, pres, freq, 0, kRefreshTile + 1, n_ready, s, best, bidx);
+      // CTA-wide refresh: the K-th largest over every warp's candidates so far
+      // is a lower bound of the CTA's K-th largest; all warps filter with it.
+      uint32_t key[kPerLane];
+#pragma unroll
+      for (int q = 0; q < kPerLane; ++q) {
+        const int i = q * 32 + lane;
+        key[q] = (i < s.n && !s.ovf) ? f2key(s.x[i]) : 0u;
+      }
+      uint32_t kk = 0;
+      if (block_kth_regs(m, key, c.K, &kk)) {
+        s.tau = fmaxf(s.tau, scaled_lower_bound(key2f(kk), c.Tabs));
+        if (!s.ovf) warp_drop_below(s);
+      }
+      if (ok) ok = stream_warp(c, mode, policy, rep, pres, freq, kRefreshTile + 1, INT_MAX, n_ready, s, best, bidx);
+    } else {
+      ok = stream_warp(c, mode, policy, rep, pres, freq, 0, INT_MAX, n_ready, s, best, bidx);
     }
   }
+  if (mode == MODE_FAST && s.ovf && lane == 0) atomicOr(&m->flags, F_OVF);
   if (mode == MODE_GREEDY) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
-      const float ob = __shfl_xor_sync(kFull, g_best, o);
-      const int oi = __shfl_xor_sync(kFull, g_idx, o);
-      if (better(ob, oi, g_best, g_idx)) {
-        g_best = ob;
-        g_idx = oi;
+      const float ob = __shfl_xor_sync(kFull, best, o);
+      const int oi = __shfl_xor_sync(kFull, bidx, o);
+      if (better(ob, oi, best, bidx)) {
+        best = ob;
+        bidx = oi;
       }
     }
-    if (lane == 0) {
-      m->f_red[warp] = g_best;
-      m->i_red[warp] = g_idx;
-    }
-    __syncthreads();
-    if (tid == 0) {
-      float b = m->f_red[0];
-      int bi = m->i_red[0];
-      for (int w = 1; w < kWarps; ++w)
-        if (better(m->f_red[w], m->i_red[w], b, bi)) {
-          b = m->f_red[w];
-          bi = m->i_red[w];
-        }
-      m->g_best = b;
-      m->g_idx = bi;
-    }
+  }
+  if (lane == 0) {
+    m->wn[warp] = (mode == MODE_FAST && ok && !s.ovf) ? s.n : 0;
+    m->wbest[warp] = best;
+    m->widx[warp] = bidx;
+  }
+  __syncthreads();
+  if (tid == 0 && mode == MODE_GREEDY) {
+    float b = m->wbest[0];
+    int bi = m->widx[0];
+    for (int w = 1; w < kWarps; ++w)
+      if (better(m->wbest[w], m->widx[w], b, bi)) {
+        b = m->wbest[w];
+        bi = m->widx[w];
+      }
+    m->g_best = b;
+    m->g_idx = bi;
   }
   __syncthreads();
 
@@ -942,15 +1432,17 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
       for (int r = 0; r < CL; ++r) {
         Misc* rm = cluster.map_shared_rank(m, r);
         fl |= rm->flags;
-        m->roff[r] = tot;
         m->rc0[r] = int(min(int64_t(r) * a.per_cta, a.vocab));
-        tot += rm->n_cand;
+        for (int w = 0; w < kWarps; ++w) {
+          m->roff[r * kWarps + w] = tot;
+          tot += rm->wn[w];
+        }
         if (better(rm->g_best, rm->g_idx, b, bi)) {
           b = rm->g_best;
           bi = rm->g_idx;
         }
       }
-      m->roff[CL] = tot;
+      m->roff[CL * kWarps] = tot;
       m->flags = fl;
       if (mode == MODE_GREEDY) {
         const int st = status_from_flags(fl, true);
@@ -960,47 +1452,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
       }
     }
     __syncthreads();
-    if (mode == MODE_FAST && status_from_flags(m->flags, false) == NS_OK) {
-      const int tot = m->roff[CL];
-      auto owner = [&](int gi) {
-        int r = 0;
-        while (r + 1 < CL && m->roff[r + 1] <= gi) ++r;
-        return r;
-      };
-      uint32_t key = 0;
-      const bool have = (tot > c.K) && radix_kth(
-                                           c, c.K,
-                                           [&](auto f) {
-                                             for (int gi = tid; gi < tot; gi += kThreads) {
-                                               const int r = owner(gi);
-                                               const float* rcx = cluster.map_shared_rank(c.cx, r);
-                                               f(rcx[gi - m->roff[r]]);
-                                             }
-                                           },
-                                           &key);
-      const float thr = have ? __fdiv_rn(key2f(key), c.Tabs) : -INFINITY;
-      float* my = reinterpret_cast<float*>(c.stages);
-      int* mid = reinterpret_cast<int*>(c.stages + size_t(a.merge_cap) * 4);
-      for (int gi = tid; gi < tot; gi += kThreads) {
-        const int r = owner(gi);
-        const float* rcx = cluster.map_shared_rank(c.cx, r);
-        const int* rcid = cluster.map_shared_rank(c.cid, r);
-        const float y = __fdiv_rn(rcx[gi - m->roff[r]], c.Tabs);
-        if (y >= thr) {
-          const int pos = atomicAdd(&m->n_merge, 1);
-          if (pos < a.merge_cap) {
-            my[pos] = y;
-            mid[pos] = rcid[gi - m->roff[r]] + m->rc0[r];
-          }
-        }
-      }
-      __syncthreads();
-      if (tid == 0 && m->n_merge > a.merge_cap) {
-        m->flags |= F_OVF;
-        a.out_ids[row] = NS_ERR_CANDIDATE_OVERFLOW;
-      }
-      __syncthreads();
-    }
+    if (mode == MODE_FAST && status_from_flags(m->flags, false) == NS_OK) leader_gather(c, a, cluster, CL);
   }
   cluster.sync();
   if (rank == 0 && mode == MODE_FAST && status_from_flags(m->flags, false) == NS_OK) finalize_row(c, a, row, topp);
@@ -1010,28 +1462,19 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
 // host side
 // ---------------------------------------------------------------------------
 struct Layout {
-  uint32_t off_bar, off_cx, off_cid, off_hist, off_hkey, off_hcnt, off_bcol, off_bcnt, off_bx, off_toff,
-      off_tfill, off_misc, total;
+  uint32_t off_bar, off_cand, off_bcol, off_bcnt, off_bx, off_toff, off_tfill, off_misc, total;
 };
 
 static uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
-static Layout make_layout(int hash_slots, int uniq_cap, int tiles_max) {
+static Layout make_layout(int hash_slots, int uniq_cap, int n_tiles_all) {
   Layout L;
-  uint32_t o = kStages * kStageStride;
+  uint32_t o = kStageBytes;
   L.off_bar = o;
-  o += kStages * 8;
+  o += kWarps * kWStages * 8;
   o = align_up(o, 16);
-  L.off_cx = o;
-  o += kCap * 4;
-  L.off_cid = o;
-  o += kCap * 4;
-  L.off_hist = o;
-  o += kBins * 4;
-  L.off_hkey = o;
-  o += hash_slots * 4;
-  L.off_hcnt = o;
-  o += hash_slots * 4;
+  L.off_cand = o;  // candidate buffers, aliased by the history hash in the prologue
+  o += std::max<uint32_t>(kCandBytes, uint32_t(hash_slots) * 8);
   L.off_bcol = o;
   o += uniq_cap * 4;
   L.off_bcnt = o;
@@ -1039,9 +1482,9 @@ static Layout make_layout(int hash_slots, int uniq_cap, int tiles_max) {
   L.off_bx = o;
   o += uniq_cap * 4;
   L.off_toff = o;
-  o += (tiles_max + 1) * 4;
+  o += (n_tiles_all + 1) * 4;
   L.off_tfill = o;
-  o += (tiles_max + 1) * 4;
+  o += (n_tiles_all + 1) * 4;
   o = align_up(o, 16);
   L.off_misc = o;
   o += sizeof(Misc);
@@ -1076,28 +1519,28 @@ static int launch(const KArgs& base, int64_t batch, ns_stream_t stream) {
   }
   KArgs a = base;
   const int64_t V = a.vocab;
-  // CTAs per row: enough rows x CTAs to cover the SMs, each CTA >= 2 tiles.
+  // CTAs per row: enough rows x CTAs to cover the SMs, each warp >= 2 tiles.
   int CL = 1;
-  while (CL < kMaxCluster && batch * CL < di->sms && V / (2 * CL) >= C_::TE) CL *= 2;
+  while (CL < kMaxCluster && batch * CL < di->sms && V / (2 * CL) >= int64_t(kWarps) * 2 * C_::TE) CL *= 2;
   int64_t per = (V + CL - 1) / CL;
   per = (per + C_::VE - 1) / C_::VE * C_::VE;
+  int64_t pw = (per + kWarps - 1) / kWarps;
+  pw = (pw + C_::VE - 1) / C_::VE * C_::VE;
   a.per_cta = int(per);
-  a.tiles_max = int((per + C_::TE - 1) / C_::TE);
+  a.per_warp = int(pw);
+  a.tpw = int((pw + C_::TE - 1) / C_::TE);
+  const int n_tiles_all = kWarps * a.tpw;
   int64_t hmax = 0;
   if (a.hist_ids) hmax = std::min<int64_t>(a.max_history, per);
   int slots = 32;
   while (slots < 2 * hmax && slots < kHashMax) slots <<= 1;
   a.hash_slots = slots;
   a.uniq_cap = int(std::min<int64_t>(std::max<int64_t>(hmax, 1), slots));
-  const Layout L = make_layout(a.hash_slots, a.uniq_cap, a.tiles_max);
+  const Layout L = make_layout(a.hash_slots, a.uniq_cap, n_tiles_all);
   a.merge_cap = 1;
-  while (a.merge_cap * 2 * 16 <= kStages * kStageStride) a.merge_cap <<= 1;
+  while (a.merge_cap * 2 * 16 <= kStageBytes) a.merge_cap <<= 1;
   a.off_bar = L.off_bar;
-  a.off_cx = L.off_cx;
-  a.off_cid = L.off_cid;
-  a.off_hist = L.off_hist;
-  a.off_hkey = L.off_hkey;
-  a.off_hcnt = L.off_hcnt;
+  a.off_cand = L.off_cand;
   a.off_bcol = L.off_bcol;
   a.off_bcnt = L.off_bcnt;
   a.off_bx = L.off_bx;
@@ -1186,6 +1629,7 @@ int ns_sample(const void* logits, int dtype, int64_t batch, int64_t vocab, int64
   a.vocab_total = vocab;
   a.hist_ids = hist_ids;
   a.hist_offsets = hist_offsets;
+  a.max_history = max_history;
   a.temperature = temperature;
   a.top_k = top_k;
   a.top_p = top_p;
@@ -1196,7 +1640,6 @@ int ns_sample(const void* logits, int dtype, int64_t batch, int64_t vocab, int64
   a.seed = philox_seed;
   a.offset = philox_offset;
   a.out_ids = out_ids;
-  a.max_history = max_history;
   switch (dtype) {
     case NS_DTYPE_F32: return ns::launch<NS_DTYPE_F32>(a, batch, stream);
     case NS_DTYPE_BF16: return ns::launch<NS_DTYPE_BF16>(a, batch, stream);
