@@ -119,6 +119,15 @@ struct Misc {
   int widx[kWarps];
   double d_red[kWarps];
   int i_red[kWarps];
+  // GENERAL rows (cluster-cooperative multi-pass)
+  unsigned g_maxk;              // this CTA's max key of x (finite values)
+  int g_bin;                    // digit search: crossing bin (-1: none)
+  unsigned long long g_before;  // digit search: cumulative value above the crossing bin
+  unsigned long long g_mass;    // this CTA's (kept) mass, fixed point
+  unsigned long long g_sum[kWarps];
+  int g_ties;                   // this CTA's count of values equal to the top-p cut
+  int g_tile;                   // inverse CDF: chosen tile of this CTA (-1: none)
+  unsigned long long g_tbefore; // ... and the kept mass before it
   int roff[kMaxLists + 1];  // leader: union offsets over (rank, warp) lists
   int rc0[kMaxCluster];     // leader: first column of each rank
   uint32_t hist[kBins];
@@ -149,7 +158,7 @@ struct KArgs {
   int hash_slots;  // power of two
   int uniq_cap;    // distinct ids the bucket arrays hold
   int merge_cap;   // leader merge area (entries)
-  uint32_t off_bar, off_cand, off_bcol, off_bcnt, off_bx, off_toff, off_tfill, off_misc;
+  uint32_t off_bar, off_cand, off_bcol, off_bcnt, off_bx, off_toff, off_tfill, off_tacc, off_misc;
 };
 
 template <int DT>
@@ -170,6 +179,7 @@ struct Ctx {
   float* bx;
   int* toff;
   int* tfill;
+  void* tacc;
   Misc* m;
 
   const uint8_t* rowp;  // column 0 of this row
@@ -411,10 +421,9 @@ __device__ __forceinline__ void warp_append_bits(const Ctx<DT>& c, WarpCand& s, 
 // tail); issued by lane 0 of the owning warp
 // ---------------------------------------------------------------------------
 template <int DT>
-__device__ void issue_tile(const Ctx<DT>& c, int w, int t, uint64_t policy) {
+__device__ void issue_tile(const Ctx<DT>& c, int w, int t, int s, uint64_t policy) {
   using E = Elem<DT>;
   constexpr int ES = E::size;
-  const int s = t % kWStages;
   const int len = c.tile_len(w, t);
   const int head = c.tile_head(w, t);
   const int body = (((len - head) * ES) & ~15) / ES;
@@ -666,7 +675,7 @@ __device__ __forceinline__ bool stream_warp(const Ctx<DT>& c, int mode, uint64_t
         fast_tile<DT, false>(c, s, w, t, st);
     }
     __syncwarp();
-    if (lane == 0 && t + kWStages < nt) issue_tile(c, w, t + kWStages, policy);
+    if (lane == 0 && t + kWStages < nt) issue_tile(c, w, t + kWStages, (t + kWStages) % kWStages, policy);
   }
   return true;
 }
@@ -1157,6 +1166,546 @@ __device__ __forceinline__ void leader_gather(const Ctx<DT>& c, const KArgs& a, 
 }
 
 // ---------------------------------------------------------------------------
+// GENERAL rows: top-k disabled, top-k > kFastK, or ties that overflowed the
+// FAST buffers.  Every CTA of the cluster streams its columns several times
+// (the row is re-read), and cluster-wide reductions go through distributed
+// shared memory.  y = rn(x / T) is computed exactly for every value.
+// Probability masses exp(y - M) are accumulated in 2^-40 fixed point, so all
+// sums (histogram bins, tile sums, the final ordered scan) are exact and
+// mutually consistent.
+//
+//   P1      max of x; NaN/+inf check; 11-bit count histogram if top-k is on
+//   P2, P3  count histograms of the next 11 and 10 bits: the exact K-th value
+//   P4      Z = sum exp(y - M) over the top-k survivors, per-tile masses, and
+//           an 11-bit mass histogram of y if top-p is on
+//   P5, P6  mass histograms of the next bits: the value c at which the
+//           descending cumulative mass first exceeds p * Z, the mass above it
+//           and the number of ties at c (reference sampler.py:122-131)
+//   P7      per-tile kept mass (y > c, plus the first ties at c in id order)
+//   P8      the warp owning the tile that holds u * total reloads it and
+//           scans it in id order
+// ---------------------------------------------------------------------------
+constexpr int kGBins = 2048;                      // 11-bit digits
+constexpr double kFx = 1099511627776.0;           // 2^40: sums stay below 2^64 for vocab <= 2^24
+
+__device__ __forceinline__ unsigned long long to_fx(float e) {
+  return (unsigned long long)(double(e) * kFx);
+}
+
+// One pass of this warp over its tiles: fe(x, col) for every value (x in the
+// negated domain when T < 0, col CTA-relative), ft(t) after each tile (all
+// lanes).  `seq` counts the copies this warp has made (it selects ring slots
+// and barrier phases across passes); `pre_issued` tiles were issued already.
+template <int DT, class FElem, class FTile>
+__device__ __forceinline__ bool warp_pass(const Ctx<DT>& c, int& seq, int pre_issued, uint64_t policy, float rep,
+                                          float pres, float freq, FElem fe, FTile ft) {
+  constexpr int VE = Ctx<DT>::VE, TE = Ctx<DT>::TE;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nt = c.wtiles(w);
+  const int s0 = seq;
+  if (lane == 0)
+    for (int t = pre_issued; t < min(kWStages, nt); ++t) issue_tile(c, w, t, (s0 + t) % kWStages, policy);
+  for (int t = 0; t < nt; ++t) {
+    const int sq = s0 + t;
+    const int sidx = sq % kWStages;
+    const bool ok = __all_sync(kFull, mbar_wait_bounded(c.sbar(w, sidx), uint32_t(sq / kWStages) & 1u));
+    if (!ok) {
+      if (lane == 0) {
+        atomicOr(&c.m->flags, F_TIMEOUT);
+        for (int u = t; u < min(nt, t + kWStages); ++u)
+          mbar_wait_bounded(c.sbar(w, (s0 + u) % kWStages), uint32_t((s0 + u) / kWStages) & 1u);
+      }
+      __syncwarp();
+      seq = s0 + nt;
+      return false;
+    }
+    uint8_t* st = c.stage(w, sidx);
+    patch_tile(c, w, t, st, rep, pres, freq);
+    __syncwarp();
+    const int len = c.tile_len(w, t), lead = c.tile_lead(w, t);
+    const int n_groups = (lead + len + VE - 1) / VE;
+    const int colbase = w * c.pw + t * TE - lead;
+    for (int q = lane; q < n_groups; q += 32) {
+      float x[VE];
+      unpack16<DT>(*reinterpret_cast<const uint4*>(st + q * 16), x);
+#pragma unroll
+      for (int i = 0; i < VE; ++i) {
+        const int e = q * VE + i;
+        if (e >= lead && e < lead + len) fe(c.neg ? -x[i] : x[i], colbase + e);
+      }
+    }
+    const int gt = w * c.tpw + t;
+    for (int j = c.toff[gt] + lane; j < c.toff[gt + 1]; j += 32) fe(c.bx[j], c.bcol[j]);
+    ft(t);
+    __syncwarp();
+    if (lane == 0 && t + kWStages < nt) issue_tile(c, w, t + kWStages, (s0 + t + kWStages) % kWStages, policy);
+  }
+  seq = s0 + nt;
+  return true;
+}
+
+__device__ __forceinline__ unsigned long long warp_sum_u64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+
+// Digit search over a histogram of nb bins held by every CTA of the cluster
+// at the same shared-memory address (combined through DSMEM, ranks in order):
+// scanning from the highest bin, the first bin whose inclusive cumulative
+// value is >= target (strict: > target).  Sets m->g_bin (-1: never) and
+// m->g_before (cumulative value of the bins above it).  Exact integer sums.
+__device__ void cluster_digit(cg::cluster_group& cl, int CL, Misc* m, const unsigned long long* h, int nb,
+                              unsigned long long target, bool strict) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = nb / kThreads;  // 8 or 4 bins per thread, highest bins first
+  unsigned long long v[kGBins / kThreads];
+  unsigned long long local = 0;
+#pragma unroll
+  for (int k = 0; k < kGBins / kThreads; ++k) {
+    v[k] = 0;
+    if (k < per) {
+      const int b = nb - 1 - (tid * per + k);
+      for (int r = 0; r < CL; ++r) v[k] += cl.map_shared_rank(const_cast<unsigned long long*>(h), r)[b];
+      local += v[k];
+    }
+  }
+  unsigned long long incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long t = __shfl_up_sync(kFull, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (tid == 0) m->g_bin = -1;
+  if (lane == 31) m->g_sum[warp] = incl;
+  __syncthreads();
+  unsigned long long run = incl - local;
+  for (int w = 0; w < warp; ++w) run += m->g_sum[w];
+#pragma unroll
+  for (int k = 0; k < kGBins / kThreads; ++k) {
+    if (k < per) {
+      const unsigned long long prev = run;
+      run += v[k];
+      const bool was = strict ? prev > target : prev >= target;
+      const bool now = strict ? run > target : run >= target;
+      if (!was && now) {
+        m->g_bin = nb - 1 - (tid * per + k);
+        m->g_before = prev;
+      }
+    }
+  }
+  __syncthreads();
+}
+
+template <int DT>
+__device__ void general_row(const Ctx<DT>& c, const KArgs& a, cg::cluster_group& cl, int CL, int rank, int& seq,
+                            int pre_issued, uint64_t policy, float rep, float pres, float freq, float topp) {
+  constexpr int VE = Ctx<DT>::VE, TE = Ctx<DT>::TE;
+  Misc* m = c.m;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n_tiles_all = kWarps * c.tpw;
+  unsigned long long* gh = reinterpret_cast<unsigned long long*>(c.cx);  // kGBins bins (candidate region)
+  unsigned long long* tmass = reinterpret_cast<unsigned long long*>(c.tacc);
+  int* tties = reinterpret_cast<int*>(tmass + n_tiles_all);
+  const bool bigk = c.K > 0 && int64_t(c.K) < a.vocab_total;
+  const bool usep = topp > 0.0f && topp < 1.0f;
+  // Flags that decide control flow mid-way are only those no later pass can
+  // set (a timeout may be set by a CTA that is already one pass ahead), so
+  // every CTA takes the same branches; timeouts are checked once, in a window
+  // where no CTA streams.
+  const int hard = F_NAN | F_BADID | F_HIST;
+  auto clear_gh = [&]() {
+    for (int i = tid; i < kGBins; i += kThreads) gh[i] = 0;
+  };
+  auto cluster_flags = [&]() {
+    int f = 0;
+    for (int r = 0; r < CL; ++r) f |= cl.map_shared_rank(m, r)->flags;
+    return f;
+  };
+  auto fail = [&](int status) {
+    if (rank == 0 && tid == 0) a.out_ids[c.row] = status;
+  };
+
+  // ---- P1 ----
+  clear_gh();
+  if (tid == 0) m->g_maxk = 0u;
+  __syncthreads();
+  {
+    float lmax = -INFINITY;
+    bool bad = false;
+    warp_pass(
+        c, seq, pre_issued, policy, rep, pres, freq,
+        [&](float x, int) {
+          if (x != x || x == INFINITY) {
+            bad = true;
+          } else if (x > -INFINITY) {
+            lmax = fmaxf(lmax, x);
+            if (bigk) atomicAdd(&gh[f2key(x) >> 21], 1ull);
+          }
+        },
+        [&](int) {});
+    if (bad) atomicOr(&m->flags, F_NAN);
+    if (lmax > -INFINITY) atomicMax(&m->g_maxk, f2key(lmax));
+  }
+  __syncthreads();
+  cl.sync();
+  const int fl = cluster_flags();
+  unsigned maxk = 0;
+  for (int r = 0; r < CL; ++r) maxk = max(maxk, cl.map_shared_rank(m, r)->g_maxk);
+  if (fl & hard) {
+    cl.sync();
+    fail(status_from_flags(fl, false));
+    return;
+  }
+  if (maxk == 0u) {  // no finite value: the reference's softmax is all-NaN
+    cl.sync();
+    fail(NS_ERR_INVALID_DISTRIBUTION);
+    return;
+  }
+  const float M = __fdiv_rn(key2f(maxk), c.Tabs);
+  if (!(M < INFINITY)) {
+    cl.sync();
+    fail(NS_ERR_INVALID_DISTRIBUTION);
+    return;
+  }
+
+  // ---- P2, P3: the K-th largest x ----
+  float lo = -INFINITY;
+  if (bigk) {
+    cluster_digit(cl, CL, m, gh, kGBins, (unsigned long long)c.K, false);
+    int d0 = m->g_bin;
+    unsigned long long krem = (unsigned long long)c.K - m->g_before;
+    cl.sync();
+    if (d0 >= 0) {
+      clear_gh();
+      __syncthreads();
+      warp_pass(
+          c, seq, 0, policy, rep, pres, freq,
+          [&](float x, int) {
+            const uint32_t k = f2key(x);
+            if (x > -INFINITY && x == x && (k >> 21) == uint32_t(d0)) atomicAdd(&gh[(k >> 10) & 0x7FFu], 1ull);
+          },
+          [&](int) {});
+      __syncthreads();
+      cl.sync();
+      cluster_digit(cl, CL, m, gh, kGBins, krem, false);
+      const int d1 = m->g_bin;
+      krem -= m->g_before;
+      cl.sync();
+      clear_gh();
+      __syncthreads();
+      const uint32_t pre = (uint32_t(d0) << 11) | uint32_t(d1);
+      warp_pass(
+          c, seq, 0, policy, rep, pres, freq,
+          [&](float x, int) {
+            const uint32_t k = f2key(x);
+            if (x > -INFINITY && x == x && (k >> 10) == pre) atomicAdd(&gh[k & 0x3FFu], 1ull);
+          },
+          [&](int) {});
+      __syncthreads();
+      cl.sync();
+      cluster_digit(cl, CL, m, gh, 1024, krem, false);
+      const uint32_t kth = (pre << 10) | uint32_t(m->g_bin);
+      lo = scaled_lower_bound(key2f(kth), c.Tabs);
+      cl.sync();
+    }
+  }
+
+  // ---- P4: masses of the top-k survivors ----
+  auto surv = [&](float x) { return x >= lo && x > -INFINITY; };
+  clear_gh();
+  __syncthreads();
+  {
+    unsigned long long acc = 0;
+    warp_pass(
+        c, seq, 0, policy, rep, pres, freq,
+        [&](float x, int) {
+          if (!surv(x)) return;
+          const float y = __fdiv_rn(x, c.Tabs);
+          const unsigned long long e = to_fx(expf(__fsub_rn(y, M)));
+          acc += e;
+          if (usep) atomicAdd(&gh[f2key(y + 0.0f) >> 21], e);
+        },
+        [&](int t) {
+          const unsigned long long sum = warp_sum_u64(acc);
+          acc = 0;
+          if (lane == 0) tmass[warp * c.tpw + t] = sum;
+        });
+  }
+  __syncthreads();
+  if (tid == 0) {
+    unsigned long long z = 0;
+    for (int w = 0; w < kWarps; ++w)
+      for (int t = 0; t < c.wtiles(w); ++t) z += tmass[w * c.tpw + t];
+    m->g_mass = z;
+  }
+  __syncthreads();
+  cl.sync();
+  unsigned long long Z = 0;
+  for (int r = 0; r < CL; ++r) Z += cl.map_shared_rank(m, r)->g_mass;
+
+  // ---- P5, P6, P7: the top-p cut ----
+  bool cut = false;
+  float cval = 0.0f;
+  unsigned long long n_keep = 0, ecut = 0;
+  if (usep) {
+    const unsigned long long target0 = (unsigned long long)(double(topp) * double(Z));
+    cluster_digit(cl, CL, m, gh, kGBins, target0, true);
+    const int b0 = m->g_bin;
+    unsigned long long O = m->g_before;
+    cl.sync();
+    if (b0 >= 0) {
+      cut = true;
+      clear_gh();
+      __syncthreads();
+      warp_pass(
+          c, seq, 0, policy, rep, pres, freq,
+          [&](float x, int) {
+            if (!surv(x)) return;
+            const float y = __fdiv_rn(x, c.Tabs);
+            const uint32_t k = f2key(y + 0.0f);
+            if ((k >> 21) == uint32_t(b0)) atomicAdd(&gh[(k >> 10) & 0x7FFu], to_fx(expf(__fsub_rn(y, M))));
+          },
+          [&](int) {});
+      __syncthreads();
+      cl.sync();
+      cluster_digit(cl, CL, m, gh, kGBins, target0 - O, true);
+      const int b1 = m->g_bin;
+      O += m->g_before;
+      cl.sync();
+      clear_gh();
+      __syncthreads();
+      const uint32_t pre = (uint32_t(b0) << 11) | uint32_t(b1);
+      warp_pass(
+          c, seq, 0, policy, rep, pres, freq,
+          [&](float x, int) {
+            if (!surv(x)) return;
+            const float y = __fdiv_rn(x, c.Tabs);
+            const uint32_t k = f2key(y + 0.0f);
+            if ((k >> 10) == pre) atomicAdd(&gh[k & 0x3FFu], to_fx(expf(__fsub_rn(y, M))));
+          },
+          [&](int) {});
+      __syncthreads();
+      cl.sync();
+      cluster_digit(cl, CL, m, gh, 1024, target0 - O, true);
+      const int b2 = m->g_bin;
+      O += m->g_before;
+      cval = key2f((pre << 10) | uint32_t(b2));
+      ecut = to_fx(expf(__fsub_rn(cval, M)));
+      unsigned long long binmass = 0;
+      for (int r = 0; r < CL; ++r) binmass += cl.map_shared_rank(gh, r)[b2];
+      const unsigned long long n_c = ecut ? binmass / ecut : 0;
+      n_keep = ecut ? min(n_c, (target0 - O) / ecut + 1) : n_c;
+      cl.sync();
+      // P7: mass above the cut and ties at it, per tile
+      {
+        unsigned long long acc = 0;
+        int ties = 0;
+        warp_pass(
+            c, seq, 0, policy, rep, pres, freq,
+            [&](float x, int) {
+              if (!surv(x)) return;
+              const float y = __fdiv_rn(x, c.Tabs) + 0.0f;
+              if (y > cval)
+                acc += to_fx(expf(__fsub_rn(y, M)));
+              else if (y == cval)
+                ++ties;
+            },
+            [&](int t) {
+              const unsigned long long sum = warp_sum_u64(acc);
+              const int tt = __reduce_add_sync(kFull, unsigned(ties));
+              acc = 0;
+              ties = 0;
+              if (lane == 0) {
+                tmass[warp * c.tpw + t] = sum;
+                tties[warp * c.tpw + t] = tt;
+              }
+            });
+      }
+      __syncthreads();
+      if (tid == 0) {
+        int tsum = 0;
+        for (int w = 0; w < kWarps; ++w)
+          for (int t = 0; t < c.wtiles(w); ++t) tsum += tties[w * c.tpw + t];
+        m->g_ties = tsum;
+      }
+      __syncthreads();
+      cl.sync();
+      unsigned long long tb = 0;  // ties in the CTAs before this one (column order)
+      for (int r = 0; r < rank; ++r) tb += (unsigned long long)cl.map_shared_rank(m, r)->g_ties;
+      if (tid == 0) {  // kept mass per tile: above the cut + the first n_keep ties in id order
+        unsigned long long z = 0;
+        for (int w = 0; w < kWarps; ++w)
+          for (int t = 0; t < c.wtiles(w); ++t) {
+            const int gt = w * c.tpw + t;
+            const unsigned long long nt = (unsigned long long)tties[gt];
+            const unsigned long long kept = (n_keep > tb) ? min(nt, n_keep - tb) : 0ull;
+            tmass[gt] += kept * ecut;
+            tties[gt] = int(tb);  // ties before this tile, for P8
+            tb += nt;
+            z += tmass[gt];
+          }
+        m->g_mass = z;
+      }
+      __syncthreads();
+      cl.sync();
+    }
+  }
+  // ---- inverse CDF: CTA, tile, then P8 inside the tile ----
+  const bool timed_out = (cluster_flags() & F_TIMEOUT) != 0;
+  unsigned long long ZS = 0;
+  for (int r = 0; r < CL; ++r) ZS += cl.map_shared_rank(m, r)->g_mass;
+  const float u = a.uniforms ? a.uniforms[c.row] : philox_uniform(a.seed, a.offset, uint64_t(c.row));
+  const unsigned long long target = (unsigned long long)(double(u) * double(ZS));
+  int rsel = -1, rlast = -1;
+  unsigned long long rbefore = 0, run = 0;
+  for (int r = 0; r < CL; ++r) {
+    const unsigned long long mr = cl.map_shared_rank(m, r)->g_mass;
+    if (mr > 0) rlast = r;
+    if (rsel < 0 && run + mr > target) {
+      rsel = r;
+      rbefore = run;
+    }
+    run += mr;
+  }
+  bool past_end = false;
+  if (rsel < 0) {  // u * total at or beyond the last step: the last kept value
+    rsel = rlast;
+    past_end = true;
+  }
+  cl.sync();  // nobody reads remote shared memory past this point
+  if (timed_out) {
+    fail(NS_ERR_DEVICE_TIMEOUT);
+    return;
+  }
+  if (rank != rsel) return;
+  if (tid == 0) {
+    int tsel = -1, tlast = -1;
+    unsigned long long tbefore = rbefore, tr = rbefore;
+    for (int w = 0; w < kWarps; ++w)
+      for (int t = 0; t < c.wtiles(w); ++t) {
+        const int gt = w * c.tpw + t;
+        if (tmass[gt] > 0) tlast = gt;
+        if (tsel < 0 && !past_end && tr + tmass[gt] > target) {
+          tsel = gt;
+          tbefore = tr;
+        }
+        tr += tmass[gt];
+      }
+    if (tsel < 0) {
+      tsel = tlast;
+      past_end = true;
+    }
+    m->g_tile = tsel;
+    m->g_tbefore = tbefore;
+    m->g_bin = past_end ? 1 : 0;
+  }
+  __syncthreads();
+  const int gsel = m->g_tile;
+  if (gsel < 0 || warp != gsel / c.tpw) return;
+  // P8: this warp reloads its tile and scans it in id order
+  const int t = gsel % c.tpw;
+  const bool pe = m->g_bin != 0;
+  const unsigned long long tbefore = m->g_tbefore;
+  const int sidx = seq % kWStages;
+  if (lane == 0) issue_tile(c, warp, t, sidx, policy);
+  if (!__all_sync(kFull, mbar_wait_bounded(c.sbar(warp, sidx), uint32_t(seq / kWStages) & 1u))) {
+    if (lane == 0) a.out_ids[c.row] = NS_ERR_DEVICE_TIMEOUT;
+    return;
+  }
+  uint8_t* st = c.stage(warp, sidx);
+  patch_tile(c, warp, t, st, rep, pres, freq);
+  __syncwarp();
+  float* F = reinterpret_cast<float*>(c.cx);  // fp32 values of the tile in column order
+  const int len = c.tile_len(warp, t), lead = c.tile_lead(warp, t);
+  const int n_groups = (lead + len + VE - 1) / VE;
+  const int base = warp * c.pw + t * TE;
+  for (int q = lane; q < n_groups; q += 32) {
+    float x[VE];
+    unpack16<DT>(*reinterpret_cast<const uint4*>(st + q * 16), x);
+#pragma unroll
+    for (int i = 0; i < VE; ++i) {
+      const int e = q * VE + i;
+      if (e >= lead && e < lead + len) F[e - lead] = c.neg ? -x[i] : x[i];
+    }
+  }
+  __syncwarp();
+  for (int j = c.toff[gsel] + lane; j < c.toff[gsel + 1]; j += 32) F[c.bcol[j] - base] = c.bx[j];
+  __syncwarp();
+  const unsigned long long ties_before = cut ? (unsigned long long)tties[gsel] : 0ull;
+  auto mass_of = [&](float x, bool& tie) {
+    tie = false;
+    if (!surv(x)) return 0ull;
+    const float y = __fdiv_rn(x, c.Tabs) + 0.0f;
+    if (cut) {
+      if (y < cval) return 0ull;
+      if (y == cval) {
+        tie = true;
+        return ecut;
+      }
+    }
+    return to_fx(expf(__fsub_rn(y, M)));
+  };
+  const int per = (len + 31) / 32;
+  const int i0 = min(lane * per, len), i1 = min(i0 + per, len);
+  unsigned long long lm = 0;
+  int lt = 0;
+  for (int i = i0; i < i1; ++i) {
+    bool tie;
+    const unsigned long long e = mass_of(F[i], tie);
+    if (tie) {
+      ++lt;
+    } else {
+      lm += e;
+    }
+  }
+  int lt_ex = lt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(kFull, lt_ex, o);
+    if (lane >= o) lt_ex += v;
+  }
+  lt_ex -= lt;
+  // kept ties of this lane's chunk are those with global tie rank < n_keep
+  unsigned long long rank0 = ties_before + (unsigned long long)lt_ex;
+  unsigned long long kept_here = 0;
+  if (cut && lt > 0 && n_keep > rank0) kept_here = min((unsigned long long)lt, n_keep - rank0);
+  lm += kept_here * ecut;
+  unsigned long long lm_ex = lm;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long v = __shfl_up_sync(kFull, lm_ex, o);
+    if (lane >= o) lm_ex += v;
+  }
+  lm_ex -= lm;
+  unsigned long long cum = tbefore + lm_ex, trank = rank0;
+  int pick = -1, last = -1;
+  for (int i = i0; i < i1; ++i) {
+    bool tie;
+    unsigned long long e = mass_of(F[i], tie);
+    if (tie) {
+      e = (trank < n_keep) ? ecut : 0ull;
+      ++trank;
+    }
+    if (e == 0) continue;
+    last = i;
+    if (pick < 0 && !pe && cum + e > target) pick = i;
+    cum += e;
+  }
+  // the first lane holding the crossing wins; past the end: the last kept value
+  const unsigned pm = __ballot_sync(kFull, pick >= 0);
+  int col = -1;
+  if (pm) {
+    col = __shfl_sync(kFull, pick, __ffs(pm) - 1);
+  } else {
+    const unsigned lmk = __ballot_sync(kFull, last >= 0);
+    if (lmk) col = __shfl_sync(kFull, last, 31 - __clz(lmk));
+  }
+  if (lane == 0)
+    a.out_ids[c.row] = (col >= 0) ? int64_t(c.c0 + base + col) + a.vocab_offset : int64_t(NS_ERR_INVALID_DISTRIBUTION);
+}
+
+// ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
 template <int DT>
@@ -1182,6 +1731,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
   c.bx = reinterpret_cast<float*>(smem + a.off_bx);
   c.toff = reinterpret_cast<int*>(smem + a.off_toff);
   c.tfill = reinterpret_cast<int*>(smem + a.off_tfill);
+  c.tacc = smem + a.off_tacc;
   c.m = reinterpret_cast<Misc*>(smem + a.off_misc);
   Misc* m = c.m;
 
@@ -1206,7 +1756,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     h0 = a.hist_offsets[row];
     h1 = a.hist_offsets[row + 1];
   }
-  const bool pen = (h1 > h0) && (rep != 1.0f || pres != 0.0f || freq != 0.0f) && mode != MODE_GENERAL;
+  const bool pen = (h1 > h0) && (rep != 1.0f || pres != 0.0f || freq != 0.0f);
   c.rowp = reinterpret_cast<const uint8_t*>(a.logits) + size_t(row) * size_t(a.row_stride) * C_::ES;
   c.row = row;
   c.c0 = int(min(int64_t(rank) * a.per_cta, a.vocab));
@@ -1218,7 +1768,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
   if (tid == 0) {
     for (int s = 0; s < kWarps * kWStages; ++s) mbar_init(&c.bar[s], 1);
     fence_mbar_init();
-    m->flags = (mode == MODE_GENERAL) ? F_UNSUP : 0;
+    m->flags = 0;
     m->n_unique = 0;
     m->n_merge = 0;
     m->choose = INT_MAX;
@@ -1237,11 +1787,11 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
   __syncthreads();
 
   const uint64_t policy = l2_policy_evict_first();
-  const bool streams = (mode != MODE_GENERAL);
+  const bool streams = (mode != MODE_GENERAL);  // GENERAL rows stream in general_row()
   // each warp starts its first copies now so they overlap the history prologue
-  if (streams && lane == 0) {
+  if (lane == 0) {
     const int nt = c.wtiles(warp);
-    for (int t = 0; t < min(kWStages, nt); ++t) issue_tile(c, warp, t, policy);
+    for (int t = 0; t < min(kWStages, nt); ++t) issue_tile(c, warp, t, t, policy);
   }
 
   // ---- history: distinct in-range ids with counts, bucketed by warp tile ----
@@ -1424,6 +1974,23 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
 
   // ---- cluster merge ----
   cluster.sync();
+  {
+    // GENERAL rows, and FAST rows whose ties overflowed a buffer anywhere in
+    // the cluster, continue with the multi-pass path (a cluster-uniform
+    // decision: every CTA reads every CTA's flags).
+    int fl_all = 0;
+    for (int r = 0; r < CL; ++r) fl_all |= cluster.map_shared_rank(m, r)->flags;
+    const bool hard = (fl_all & (F_NAN | F_TIMEOUT | F_BADID | F_HIST)) != 0;
+    if (mode == MODE_GENERAL || (mode == MODE_FAST && (fl_all & F_OVF) && !hard)) {
+      cluster.sync();
+      if (tid == 0) m->flags &= ~F_OVF;
+      __syncthreads();
+      int seq = (mode == MODE_GENERAL) ? 0 : c.wtiles(warp);
+      const int pre = (mode == MODE_GENERAL) ? min(kWStages, c.wtiles(warp)) : 0;
+      general_row(c, a, cluster, CL, rank, seq, pre, policy, rep, pres, freq, topp);
+      return;
+    }
+  }
   if (rank == 0) {
     if (tid == 0) {
       int fl = 0, tot = 0;
@@ -1462,7 +2029,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
 // host side
 // ---------------------------------------------------------------------------
 struct Layout {
-  uint32_t off_bar, off_cand, off_bcol, off_bcnt, off_bx, off_toff, off_tfill, off_misc, total;
+  uint32_t off_bar, off_cand, off_bcol, off_bcnt, off_bx, off_toff, off_tfill, off_tacc, off_misc, total;
 };
 
 static uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
@@ -1485,6 +2052,9 @@ static Layout make_layout(int hash_slots, int uniq_cap, int n_tiles_all) {
   o += (n_tiles_all + 1) * 4;
   L.off_tfill = o;
   o += (n_tiles_all + 1) * 4;
+  o = align_up(o, 16);
+  L.off_tacc = o;  // GENERAL: per-(warp, tile) mass (fp64) and tie count
+  o += n_tiles_all * 12;
   o = align_up(o, 16);
   L.off_misc = o;
   o += sizeof(Misc);
@@ -1546,6 +2116,7 @@ static int launch(const KArgs& base, int64_t batch, ns_stream_t stream) {
   a.off_bx = L.off_bx;
   a.off_toff = L.off_toff;
   a.off_tfill = L.off_tfill;
+  a.off_tacc = L.off_tacc;
   a.off_misc = L.off_misc;
   if (int(L.total) > di->max_smem_optin) return NS_ERR_INVALID_ARGUMENT;
   {
@@ -1617,7 +2188,7 @@ int ns_sample(const void* logits, int dtype, int64_t batch, int64_t vocab, int64
   (void)workspace_bytes;
   if (dtype != NS_DTYPE_F32 && dtype != NS_DTYPE_BF16 && dtype != NS_DTYPE_F16) return NS_ERR_UNSUPPORTED_DTYPE;
   if (batch < 0 || vocab <= 0 || row_stride < vocab || max_history < 0) return NS_ERR_INVALID_ARGUMENT;
-  if (vocab > (int64_t(1) << 30) || batch > (int64_t(1) << 24)) return NS_ERR_INVALID_ARGUMENT;
+  if (vocab > (int64_t(1) << 24) || batch > (int64_t(1) << 24)) return NS_ERR_INVALID_ARGUMENT;
   if ((hist_ids == nullptr) != (hist_offsets == nullptr)) return NS_ERR_INVALID_ARGUMENT;
   if (batch == 0) return NS_OK;
   if (!logits || !temperature || !top_k || !top_p || !out_ids) return NS_ERR_INVALID_ARGUMENT;
