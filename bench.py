@@ -197,8 +197,31 @@ def run_reference(args, world, rank):
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
-def run_ours(args, world, rank, local):
+def run_e2e(args, world, w, dev, stream):
     from b200_sampler import B200Sampler
+    B, V, H = w.batch, w.vocab, w.history_len
+    sampler = B200Sampler(device=dev, seed=1)
+    host_logits = w.logits.pin_memory()
+    hists = w.histories
+    u_host = w.uniforms
+    e2e_steps = max(1, min(args.steps, 10))
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            sampler.select_batch(host_logits, hists, w.params, uniforms=u_host)
+        barrier(world)
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            ids = sampler.select_batch(host_logits, hists, w.params, uniforms=u_host)
+        dt = time.perf_counter() - t0
+    dt = max_over_ranks(world, dt)
+    assert len(ids) == B
+    return {"value": B * world * e2e_steps / dt, "unit": UNIT,
+            "h2d_bytes_per_step": B * V * 4 + B * H * 4 + (B + 1) * 8 + B * 24 + B * 4,
+            "d2h_bytes_per_step": B * 8, "steps": e2e_steps,
+            "path": "B200Sampler.select_batch(pinned host logits, List[List[int]] histories) -> List[int]"}
+
+
+def run_ours(args, world, rank, local):
     from b200_sampler.sampler import DeviceBatch
     from b200_sampler.workloads import headline
 
@@ -256,25 +279,9 @@ def run_ours(args, world, rank, local):
     del g
 
     # ---- end to end through the public API, host buffers ----
-    sampler = B200Sampler(device=dev, seed=1)
-    host_logits = w.logits.pin_memory()
-    hists = w.histories
-    u_host = w.uniforms
-    e2e_steps = max(1, min(args.steps, 10))
-    with torch.cuda.stream(stream):
-        for _ in range(2):
-            sampler.select_batch(host_logits, hists, w.params, uniforms=u_host)
-        barrier(world)
-        t0 = time.perf_counter()
-        for _ in range(e2e_steps):
-            ids = sampler.select_batch(host_logits, hists, w.params, uniforms=u_host)
-        dt = time.perf_counter() - t0
-    dt = max_over_ranks(world, dt)
-    assert len(ids) == B
-    e2e = {"value": B * world * e2e_steps / dt, "unit": UNIT,
-           "h2d_bytes_per_step": B * V * 4 + B * H * 4 + (B + 1) * 8 + B * 24 + B * 4,
-           "d2h_bytes_per_step": B * 8, "steps": e2e_steps,
-           "path": "B200Sampler.select_batch(pinned host logits, List[List[int]] histories) -> List[int]"}
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, world, w, dev, stream)
 
     line = {"metric": METRIC, "value": tokens_per_s, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
@@ -286,8 +293,9 @@ def run_ours(args, world, rank, local):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": alg},
-            "gpu_launches": args.steps,
-            "e2e": e2e}
+            "gpu_launches": args.steps}
+    if e2e is not None:
+        line["e2e"] = e2e
     clocks = clk.summary()
     if clocks is not None:
         line["clocks"] = clocks
@@ -307,6 +315,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
     args = ap.parse_args()
     world, rank, local = (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
                           int(os.environ.get("LOCAL_RANK", "0")))

@@ -67,7 +67,6 @@ constexpr int kCandBytes = kWarps * kCapW * 8;  // candidate buffers (x, col)
 constexpr int kBins = 256;                      // radix digit = 8 bits (one bin per thread)
 static_assert(kBins == kThreads, "block_kth_regs clears one bin per thread");
 constexpr int kRefreshTile = 3;                 // FAST: CTA-wide threshold refresh after this warp tile
-constexpr int kHashMax = 8192;                  // distinct history ids per CTA (power of two)
 constexpr int kMaxCluster = 8;
 constexpr int kMaxLists = kMaxCluster * kWarps;
 constexpr unsigned kFull = 0xFFFFFFFFu;
@@ -107,7 +106,6 @@ struct Elem<NS_DTYPE_F16> {
 // ---------------------------------------------------------------------------
 struct Misc {
   int flags;      // F_* bits of this CTA (the leader's becomes the cluster's)
-  int n_unique;   // distinct history ids in this CTA's columns
   int r_digit;    // radix-select broadcast
   int r_krem;
   int n_merge;    // leader: survivors gathered from the cluster
@@ -155,10 +153,11 @@ struct KArgs {
   int per_cta;     // columns per CTA (multiple of the 16-byte vector width)
   int per_warp;    // columns per warp (multiple of the 16-byte vector width)
   int tpw;         // tiles per warp (upper bound)
-  int hash_slots;  // power of two
-  int uniq_cap;    // distinct ids the bucket arrays hold
+  int nwords;      // history bitmap words (one bit per column of a CTA)
+  int nsb;         // 256-column superblocks of the bitmap
+  int cnt_cap;     // distinct history ids the count array holds
   int merge_cap;   // leader merge area (entries)
-  uint32_t off_bar, off_cand, off_bcol, off_bcnt, off_bx, off_toff, off_tfill, off_tacc, off_misc;
+  uint32_t off_bar, off_cand, off_bits, off_sbp, off_cnt, off_tacc, off_misc;
 };
 
 template <int DT>
@@ -172,13 +171,9 @@ struct Ctx {
   uint64_t* bar;
   float* cx;  // [kWarps][kCapW]
   int* cid;   // [kWarps][kCapW]
-  int* hkey;  // aliases the candidate buffers during the prologue
-  int* hcnt;
-  int* bcol;
-  int* bcnt;
-  float* bx;
-  int* toff;
-  int* tfill;
+  uint32_t* bits;  // history membership, one bit per CTA column
+  uint32_t* sbp;   // set bits before each 256-column superblock
+  int* cnt;        // occurrences of each distinct history id, by bit rank
   void* tacc;
   Misc* m;
 
@@ -186,8 +181,10 @@ struct Ctx {
   int64_t row;
   int c0, c1;           // this CTA's columns
   int pw, tpw;          // per-warp columns / tiles
+  int nwords;
   int K;
   bool neg;
+  bool pen;  // this row has a history and a non-neutral penalty
   float Tabs;
 
   __device__ __forceinline__ int w0(int w) const { return min(c0 + w * pw, c1); }
@@ -438,29 +435,67 @@ __device__ void issue_tile(const Ctx<DT>& c, int w, int t, int s, uint64_t polic
   if (bytes) bulk_g2s(d + lead + head, src + head, bytes, c.sbar(w, s), policy);
 }
 
-// Penalise the history columns of warp tile (w, t) in place: the penalised
-// value goes to bx[], the shared-memory slot becomes -inf (in the negated
-// domain when T < 0).  Called by all lanes of the owning warp.
-template <int DT>
+// Penalise the history columns of warp tile (w, t).  Lane l reads the bitmap
+// words of tile columns [32 * (l + 32 k), +32); every set bit is a distinct
+// history id whose occurrence count is cnt[rank of the bit].  The penalised
+// value (negated when T < 0) goes to emit(has, x, col) -- called by all 32
+// lanes once per round, `has` false for lanes without a value, col relative
+// to the CTA's first column -- and the shared-memory slot becomes -inf so the
+// tile's own pass skips it.
+template <int DT, class Emit>
 __device__ __forceinline__ void patch_tile(const Ctx<DT>& c, int w, int t, uint8_t* st, float rep, float pres,
-                                           float freq) {
+                                           float freq, Emit emit) {
   using E = Elem<DT>;
   using R = typename E::raw;
-  const int gt = w * c.tpw + t;
-  const int b0 = c.toff[gt], b1 = c.toff[gt + 1];
-  if (b0 == b1) return;
-  R* sr = reinterpret_cast<R*>(st);
-  const int lead = c.tile_lead(w, t);
-  const int base = w * c.pw + t * Ctx<DT>::TE;  // CTA-relative column of the tile's first element
+  constexpr int TE = Ctx<DT>::TE;
+  constexpr int WPL = TE / 32 / 32;  // bitmap words per lane per tile (1 or 2)
+  if (!c.pen) return;
   const int lane = threadIdx.x & 31;
-  for (int j = b0 + lane; j < b1; j += 32) {
-    const int e = lead + c.bcol[j] - base;
-    float xp = penalize(E::widen(sr[e]), c.bcnt[j], rep, pres, freq);
-    if (c.neg) xp = -xp;
-    c.bx[j] = xp;
-    sr[e] = c.neg ? E::pinf : E::ninf;
+  const int base = w * c.pw + t * TE;  // a multiple of 32
+  const int len = c.tile_len(w, t), lead = c.tile_lead(w, t);
+  R* sr = reinterpret_cast<R*>(st);
+  uint32_t word[WPL], rem[WPL], rb[WPL];
+  bool any = false;
+#pragma unroll
+  for (int k = 0; k < WPL; ++k) {
+    const int off = (lane + 32 * k) * 32;  // tile column of the word's first bit
+    const int wi = (base + off) >> 5;
+    word[k] = (off < len && wi < c.nwords) ? c.bits[wi] : 0u;
+    rem[k] = word[k];
+    rb[k] = 0;
+    any |= word[k] != 0u;
   }
-  fence_proxy_async_smem();
+  if (!__any_sync(kFull, any)) return;
+#pragma unroll
+  for (int k = 0; k < WPL; ++k)
+    if (word[k]) {
+      const int wi = (base + (lane + 32 * k) * 32) >> 5;
+      uint32_t r = c.sbp[wi >> 3];
+      for (int j = wi & ~7; j < wi; ++j) r += __popc(c.bits[j]);
+      rb[k] = r;
+    }
+  while (true) {
+    bool has = false;
+    float xp = 0.0f;
+    int col = 0;
+#pragma unroll
+    for (int k = 0; k < WPL; ++k)
+      if (!has && rem[k]) {
+        const int b = __ffs(rem[k]) - 1;
+        const int off = (lane + 32 * k) * 32 + b;
+        col = base + off;
+        const int e = lead + off;
+        const int count = c.cnt[rb[k] + __popc(word[k] & ((1u << b) - 1u))];
+        xp = penalize(E::widen(sr[e]), count, rep, pres, freq);
+        if (c.neg) xp = -xp;
+        sr[e] = c.neg ? E::pinf : E::ninf;
+        rem[k] &= rem[k] - 1u;
+        has = true;
+      }
+    if (!__any_sync(kFull, has)) break;
+    emit(has, xp, col);
+  }
+  fence_proxy_async_smem();  // the slot is rewritten by a later bulk copy
 }
 
 // ---------------------------------------------------------------------------
@@ -574,18 +609,15 @@ __device__ __forceinline__ void fast_tile(const Ctx<DT>& c, WarpCand& s, int w, 
     if (__any_sync(kFull, !ca)) group_append(c, s, qa, xa, !ca, lead, len, n_groups, colbase);
     if (__any_sync(kFull, !cb)) group_append(c, s, qb, xb, !cb, lead, len, n_groups, colbase);
   }
-  const int gt = w * c.tpw + t;
-  const int b0 = c.toff[gt], b1 = c.toff[gt + 1];
-  for (int j0 = b0; j0 < b1; j0 += 32) {
-    const int j = j0 + lane;
-    const bool in = j < b1;
-    const float xb1[1] = {in ? c.bx[j] : -INFINITY};
-    const int col = in ? c.bcol[j] : 0;
-    const bool bad = in && (xb1[0] != xb1[0] || xb1[0] == INFINITY);
-    if (bad) atomicOr(&c.m->flags, F_NAN);
-    const bool want = in && !bad && xb1[0] >= s.tau && xb1[0] > -INFINITY;
-    warp_append_bits(c, s, want ? 1u : 0u, xb1, col);
-  }
+}
+
+// FAST handling of one penalised history value (all lanes, one per lane).
+template <int DT>
+__device__ __forceinline__ void fast_emit(const Ctx<DT>& c, WarpCand& s, bool has, float xp, int col) {
+  const bool bad = has && (xp != xp || xp == INFINITY);
+  if (bad) atomicOr(&c.m->flags, F_NAN);
+  const float v[1] = {xp};
+  warp_append_bits(c, s, (has && !bad && xp >= s.tau && xp > -INFINITY) ? 1u : 0u, v, col);
 }
 
 // GREEDY of one landed tile: per-lane running first-index argmax.  A lane sees
@@ -630,14 +662,6 @@ __device__ __forceinline__ void greedy_tile(const Ctx<DT>& c, int w, int t, cons
       greedy_group<DT>(xb, qb, lead, len, n_groups, colbase, best, bidx);
     }
   }
-  const int gt = w * c.tpw + t;
-  for (int j = c.toff[gt] + lane; j < c.toff[gt + 1]; j += 32) {
-    const int col = c.c0 + c.bcol[j];
-    if (better(c.bx[j], col, best, bidx)) {
-      best = c.bx[j];
-      bidx = col;
-    }
-  }
 }
 
 // Stream tiles [t_begin, t_end) of this warp's columns (its first kWStages
@@ -663,7 +687,16 @@ __device__ __forceinline__ bool stream_warp(const Ctx<DT>& c, int mode, uint64_t
         __syncwarp();
         return false;
       }
-      patch_tile(c, w, t, st, rep, pres, freq);
+      if (mode == MODE_GREEDY) {
+        patch_tile(c, w, t, st, rep, pres, freq, [&](bool has, float xp, int col) {
+          if (has && better(xp, c.c0 + col, best, bidx)) {
+            best = xp;
+            bidx = c.c0 + col;
+          }
+        });
+      } else if (!s.ovf) {
+        patch_tile(c, w, t, st, rep, pres, freq, [&](bool has, float xp, int col) { fast_emit(c, s, has, xp, col); });
+      }
       __syncwarp();
     }
     if (mode == MODE_GREEDY) {
@@ -678,23 +711,6 @@ __device__ __forceinline__ bool stream_warp(const Ctx<DT>& c, int mode, uint64_t
     if (lane == 0 && t + kWStages < nt) issue_tile(c, w, t + kWStages, (t + kWStages) % kWStages, policy);
   }
   return true;
-}
-
-__device__ __forceinline__ void hash_insert(int* hkey, int* hcnt, Misc* m, int key, int slots) {
-  uint32_t h = (uint32_t(key) * 2654435761u) & uint32_t(slots - 1);
-  for (int probe = 0; probe < slots; ++probe) {
-    const int prev = atomicCAS(&hkey[h], -1, key);
-    if (prev == -1) {
-      atomicAdd(&hcnt[h], 1);
-      return;
-    }
-    if (prev == key) {
-      atomicAdd(&hcnt[h], 1);
-      return;
-    }
-    h = (h + 1) & uint32_t(slots - 1);
-  }
-  atomicOr(&m->flags, F_HIST);
 }
 
 // ---------------------------------------------------------------------------
@@ -1220,7 +1236,9 @@ __device__ __forceinline__ bool warp_pass(const Ctx<DT>& c, int& seq, int pre_is
       return false;
     }
     uint8_t* st = c.stage(w, sidx);
-    patch_tile(c, w, t, st, rep, pres, freq);
+    patch_tile(c, w, t, st, rep, pres, freq, [&](bool has, float xp, int col) {
+      if (has) fe(xp, col);
+    });
     __syncwarp();
     const int len = c.tile_len(w, t), lead = c.tile_lead(w, t);
     const int n_groups = (lead + len + VE - 1) / VE;
@@ -1234,8 +1252,6 @@ __device__ __forceinline__ bool warp_pass(const Ctx<DT>& c, int& seq, int pre_is
         if (e >= lead && e < lead + len) fe(c.neg ? -x[i] : x[i], colbase + e);
       }
     }
-    const int gt = w * c.tpw + t;
-    for (int j = c.toff[gt] + lane; j < c.toff[gt + 1]; j += 32) fe(c.bx[j], c.bcol[j]);
     ft(t);
     __syncwarp();
     if (lane == 0 && t + kWStages < nt) issue_tile(c, w, t + kWStages, (s0 + t + kWStages) % kWStages, policy);
@@ -1614,12 +1630,11 @@ __device__ void general_row(const Ctx<DT>& c, const KArgs& a, cg::cluster_group&
     return;
   }
   uint8_t* st = c.stage(warp, sidx);
-  patch_tile(c, warp, t, st, rep, pres, freq);
-  __syncwarp();
   float* F = reinterpret_cast<float*>(c.cx);  // fp32 values of the tile in column order
   const int len = c.tile_len(warp, t), lead = c.tile_lead(warp, t);
   const int n_groups = (lead + len + VE - 1) / VE;
   const int base = warp * c.pw + t * TE;
+
   for (int q = lane; q < n_groups; q += 32) {
     float x[VE];
     unpack16<DT>(*reinterpret_cast<const uint4*>(st + q * 16), x);
@@ -1630,7 +1645,10 @@ __device__ void general_row(const Ctx<DT>& c, const KArgs& a, cg::cluster_group&
     }
   }
   __syncwarp();
-  for (int j = c.toff[gsel] + lane; j < c.toff[gsel + 1]; j += 32) F[c.bcol[j] - base] = c.bx[j];
+  // history columns get their penalised values on top of the raw ones
+  patch_tile(c, warp, t, st, rep, pres, freq, [&](bool has, float xp, int col) {
+    if (has) F[col - base] = xp;
+  });
   __syncwarp();
   const unsigned long long ties_before = cut ? (unsigned long long)tties[gsel] : 0ull;
   auto mass_of = [&](float x, bool& tie) {
@@ -1724,13 +1742,10 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
   c.bar = reinterpret_cast<uint64_t*>(smem + a.off_bar);
   c.cx = reinterpret_cast<float*>(smem + a.off_cand);
   c.cid = reinterpret_cast<int*>(smem + a.off_cand + kWarps * kCapW * 4);
-  c.hkey = reinterpret_cast<int*>(smem + a.off_cand);
-  c.hcnt = reinterpret_cast<int*>(smem + a.off_cand + size_t(a.hash_slots) * 4);
-  c.bcol = reinterpret_cast<int*>(smem + a.off_bcol);
-  c.bcnt = reinterpret_cast<int*>(smem + a.off_bcnt);
-  c.bx = reinterpret_cast<float*>(smem + a.off_bx);
-  c.toff = reinterpret_cast<int*>(smem + a.off_toff);
-  c.tfill = reinterpret_cast<int*>(smem + a.off_tfill);
+  c.bits = reinterpret_cast<uint32_t*>(smem + a.off_bits);
+  c.sbp = reinterpret_cast<uint32_t*>(smem + a.off_sbp);
+  c.cnt = reinterpret_cast<int*>(smem + a.off_cnt);
+  c.nwords = a.nwords;
   c.tacc = smem + a.off_tacc;
   c.m = reinterpret_cast<Misc*>(smem + a.off_misc);
   Misc* m = c.m;
@@ -1757,6 +1772,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     h1 = a.hist_offsets[row + 1];
   }
   const bool pen = (h1 > h0) && (rep != 1.0f || pres != 0.0f || freq != 0.0f);
+  c.pen = pen;
   c.rowp = reinterpret_cast<const uint8_t*>(a.logits) + size_t(row) * size_t(a.row_stride) * C_::ES;
   c.row = row;
   c.c0 = int(min(int64_t(rank) * a.per_cta, a.vocab));
@@ -1769,20 +1785,14 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     for (int s = 0; s < kWarps * kWStages; ++s) mbar_init(&c.bar[s], 1);
     fence_mbar_init();
     m->flags = 0;
-    m->n_unique = 0;
     m->n_merge = 0;
     m->choose = INT_MAX;
     m->g_best = -INFINITY;
     m->g_idx = INT_MAX;
   }
-  if (pen)
-    for (int i = tid; i < a.hash_slots; i += kThreads) {
-      c.hkey[i] = -1;
-      c.hcnt[i] = 0;
-    }
-  for (int i = tid; i <= n_tiles_all; i += kThreads) {
-    c.toff[i] = 0;
-    c.tfill[i] = 0;
+  if (pen) {
+    for (int i = tid; i < a.nwords; i += kThreads) c.bits[i] = 0u;
+    for (int i = tid; i < a.cnt_cap; i += kThreads) c.cnt[i] = 0;
   }
   __syncthreads();
 
@@ -1794,73 +1804,77 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     for (int t = 0; t < min(kWStages, nt); ++t) issue_tile(c, warp, t, t, policy);
   }
 
-  // ---- history: distinct in-range ids with counts, bucketed by warp tile ----
+  // ---- history: membership bitmap and occurrence counts ----
+  // Fire-and-forget shared atomics only: bits are set with atomicOr, the
+  // prefix popcount of every 256-column superblock gives each distinct id a
+  // rank, and the counts are accumulated with atomicAdd at that rank.
   if (pen) {
-    constexpr int kHB = 8;  // ids loaded per thread before inserting (one round trip per batch)
-    for (int64_t base = h0; base < h1; base += int64_t(kThreads) * kHB) {
-      int ids[kHB];
+    constexpr int kHB = 8;  // ids loaded per thread per round trip
+    auto for_ids = [&](auto f) {
+      for (int64_t base = h0; base < h1; base += int64_t(kThreads) * kHB) {
+        int ids[kHB];
 #pragma unroll
-      for (int q = 0; q < kHB; ++q) {
-        const int64_t i = base + int64_t(q) * kThreads + tid;
-        ids[q] = (i < h1) ? a.hist_ids[i] : INT_MIN;
-      }
-#pragma unroll
-      for (int q = 0; q < kHB; ++q) {
-        const int id = ids[q];
-        if (id == INT_MIN) continue;
-        if (id < 0 || int64_t(id) >= a.vocab_total) {
-          atomicOr(&m->flags, F_BADID);
-          continue;
+        for (int q = 0; q < kHB; ++q) {
+          const int64_t i = base + int64_t(q) * kThreads + tid;
+          ids[q] = (i < h1) ? a.hist_ids[i] : INT_MIN;
         }
-        const int64_t lc = int64_t(id) - a.vocab_offset;
-        if (lc >= c.c0 && lc < c.c1) hash_insert(c.hkey, c.hcnt, m, int(lc - c.c0), a.hash_slots);
+#pragma unroll
+        for (int q = 0; q < kHB; ++q)
+          if (ids[q] != INT_MIN) f(ids[q]);
       }
+    };
+    for_ids([&](int id) {
+      if (id < 0 || int64_t(id) >= a.vocab_total) {
+        atomicOr(&m->flags, F_BADID);
+        return;
+      }
+      const int64_t lc = int64_t(id) - a.vocab_offset;
+      if (lc >= c.c0 && lc < c.c1) {
+        const int rel = int(lc - c.c0);
+        atomicOr(&c.bits[rel >> 5], 1u << (rel & 31));
+      }
+    });
+    __syncthreads();
+    {  // exclusive prefix popcount per superblock (contiguous chunks per thread)
+      const int per = (a.nsb + kThreads - 1) / kThreads;
+      const int s0 = min(tid * per, a.nsb), s1 = min(s0 + per, a.nsb);
+      uint32_t local = 0;
+      for (int sb = s0; sb < s1; ++sb)
+        for (int j = sb * 8; j < min(sb * 8 + 8, a.nwords); ++j) local += __popc(c.bits[j]);
+      uint32_t incl = local;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t v = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += v;
+      }
+      if (lane == 31) m->i_red[warp] = int(incl);
+      __syncthreads();
+      uint32_t run = incl - local, total = 0;
+      for (int w = 0; w < kWarps; ++w) {
+        if (w < warp) run += uint32_t(m->i_red[w]);
+        total += uint32_t(m->i_red[w]);
+      }
+      for (int sb = s0; sb < s1; ++sb) {
+        c.sbp[sb] = run;
+        for (int j = sb * 8; j < min(sb * 8 + 8, a.nwords); ++j) run += __popc(c.bits[j]);
+      }
+      if (total > uint32_t(a.cnt_cap) && tid == 0) atomicOr(&m->flags, F_HIST);
     }
     __syncthreads();
-    int occupied = 0;
-    for (int i = tid; i < a.hash_slots; i += kThreads) occupied += (c.hkey[i] >= 0) ? 1 : 0;
-    const int nu = block_sum_int(m, occupied);
-    if (nu > a.uniq_cap) {
-      if (tid == 0) atomicOr(&m->flags, F_HIST);
-    } else if (nu > 0) {
-      auto tile_of = [&](int key) {
-        const int w = key / c.pw;
-        return w * c.tpw + (key - w * c.pw) / TE;
-      };
-      for (int i = tid; i < a.hash_slots; i += kThreads)
-        if (c.hkey[i] >= 0) atomicAdd(&c.tfill[tile_of(c.hkey[i])], 1);
-      __syncthreads();
-      if (warp == 0) {
-        int carry = 0;
-        for (int base = 0; base < n_tiles_all; base += 32) {
-          const int t = base + lane;
-          const int v = (t < n_tiles_all) ? c.tfill[t] : 0;
-          int incl = v;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const int w = __shfl_up_sync(kFull, incl, o);
-            if (lane >= o) incl += w;
-          }
-          if (t < n_tiles_all) {
-            c.toff[t] = carry + incl - v;
-            c.tfill[t] = 0;
-          }
-          carry += __shfl_sync(kFull, incl, 31);
+    if (!(m->flags & F_HIST)) {
+      for_ids([&](int id) {
+        const int64_t lc = int64_t(id) - a.vocab_offset;
+        if (id >= 0 && lc >= c.c0 && lc < c.c1) {
+          const int rel = int(lc - c.c0);
+          const int wi = rel >> 5, b = rel & 31;
+          uint32_t r = c.sbp[wi >> 3];
+          for (int j = wi & ~7; j < wi; ++j) r += __popc(c.bits[j]);
+          r += __popc(c.bits[wi] & ((1u << b) - 1u));
+          atomicAdd(&c.cnt[r], 1);
         }
-        if (lane == 0) c.toff[n_tiles_all] = carry;
-      }
-      __syncthreads();
-      for (int i = tid; i < a.hash_slots; i += kThreads) {
-        const int key = c.hkey[i];
-        if (key >= 0) {
-          const int t = tile_of(key);
-          const int pos = c.toff[t] + atomicAdd(&c.tfill[t], 1);
-          c.bcol[pos] = key;
-          c.bcnt[pos] = c.hcnt[i];
-        }
-      }
+      });
     }
-    __syncthreads();  // the hash is dead from here on: its memory holds the candidate buffers
+    __syncthreads();
   }
 
   // ---- stream: every warp independently ----
@@ -1888,7 +1902,10 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
       constexpr int VE = C_::VE;
       for (int t = 0; t < nr; ++t) {
         uint8_t* st = c.stage(warp, t);
-        patch_tile(c, warp, t, st, rep, pres, freq);
+        patch_tile(c, warp, t, st, rep, pres, freq, [&](bool has, float xk, int col) {
+          if (has && xk > -INFINITY && xk < INFINITY) tmax = fmaxf(tmax, xk);
+          fast_emit(c, s, has, xk, col);
+        });
         __syncwarp();
         const int len = c.tile_len(warp, t), lead = c.tile_lead(warp, t);
         const int n_groups = (lead + len + VE - 1) / VE;
@@ -1901,11 +1918,6 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
             const float xk = c.neg ? -x[i] : x[i];
             if (e >= lead && e < lead + len && xk > -INFINITY && xk < INFINITY) tmax = fmaxf(tmax, xk);
           }
-        }
-        const int gt = warp * c.tpw + t;
-        for (int j = c.toff[gt] + lane; j < c.toff[gt + 1]; j += 32) {
-          const float xk = c.bx[j];
-          if (xk > -INFINITY && xk < INFINITY) tmax = fmaxf(tmax, xk);
         }
       }
     }
@@ -2029,31 +2041,27 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
 // host side
 // ---------------------------------------------------------------------------
 struct Layout {
-  uint32_t off_bar, off_cand, off_bcol, off_bcnt, off_bx, off_toff, off_tfill, off_tacc, off_misc, total;
+  uint32_t off_bar, off_cand, off_bits, off_sbp, off_cnt, off_tacc, off_misc, total;
 };
 
 static uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
-static Layout make_layout(int hash_slots, int uniq_cap, int n_tiles_all) {
+static Layout make_layout(int nwords, int nsb, int cnt_cap, int n_tiles_all) {
   Layout L;
   uint32_t o = kStageBytes;
   L.off_bar = o;
   o += kWarps * kWStages * 8;
   o = align_up(o, 16);
-  L.off_cand = o;  // candidate buffers, aliased by the history hash in the prologue
-  o += std::max<uint32_t>(kCandBytes, uint32_t(hash_slots) * 8);
-  L.off_bcol = o;
-  o += uniq_cap * 4;
-  L.off_bcnt = o;
-  o += uniq_cap * 4;
-  L.off_bx = o;
-  o += uniq_cap * 4;
-  L.off_toff = o;
-  o += (n_tiles_all + 1) * 4;
-  L.off_tfill = o;
-  o += (n_tiles_all + 1) * 4;
+  L.off_cand = o;  // FAST candidate buffers / GENERAL histograms / tile expansion
+  o += kCandBytes;
+  L.off_bits = o;
+  o += uint32_t(nwords) * 4;
+  L.off_sbp = o;
+  o += uint32_t(nsb + 1) * 4;
+  L.off_cnt = o;
+  o += uint32_t(cnt_cap) * 4;
   o = align_up(o, 16);
-  L.off_tacc = o;  // GENERAL: per-(warp, tile) mass (fp64) and tie count
+  L.off_tacc = o;  // GENERAL: per-(warp, tile) mass (fixed point) and tie count
   o += n_tiles_all * 12;
   o = align_up(o, 16);
   L.off_misc = o;
@@ -2095,27 +2103,23 @@ static int launch(const KArgs& base, int64_t batch, ns_stream_t stream) {
   int64_t per = (V + CL - 1) / CL;
   per = (per + C_::VE - 1) / C_::VE * C_::VE;
   int64_t pw = (per + kWarps - 1) / kWarps;
-  pw = (pw + C_::VE - 1) / C_::VE * C_::VE;
+  pw = (pw + 31) / 32 * 32;  // warp ranges start on bitmap words
   a.per_cta = int(per);
   a.per_warp = int(pw);
   a.tpw = int((pw + C_::TE - 1) / C_::TE);
   const int n_tiles_all = kWarps * a.tpw;
-  int64_t hmax = 0;
-  if (a.hist_ids) hmax = std::min<int64_t>(a.max_history, per);
-  int slots = 32;
-  while (slots < 2 * hmax && slots < kHashMax) slots <<= 1;
-  a.hash_slots = slots;
-  a.uniq_cap = int(std::min<int64_t>(std::max<int64_t>(hmax, 1), slots));
-  const Layout L = make_layout(a.hash_slots, a.uniq_cap, n_tiles_all);
+  const int64_t span = int64_t(kWarps) * pw;  // columns one CTA may own
+  a.nwords = a.hist_ids ? int((span + 31) / 32) : 0;
+  a.nsb = (a.nwords + 7) / 8;
+  a.cnt_cap = a.hist_ids ? int(std::min<int64_t>(std::max<int64_t>(a.max_history, 1), span)) : 0;
+  const Layout L = make_layout(a.nwords, a.nsb, a.cnt_cap, n_tiles_all);
   a.merge_cap = 1;
   while (a.merge_cap * 2 * 16 <= kStageBytes) a.merge_cap <<= 1;
   a.off_bar = L.off_bar;
   a.off_cand = L.off_cand;
-  a.off_bcol = L.off_bcol;
-  a.off_bcnt = L.off_bcnt;
-  a.off_bx = L.off_bx;
-  a.off_toff = L.off_toff;
-  a.off_tfill = L.off_tfill;
+  a.off_bits = L.off_bits;
+  a.off_sbp = L.off_sbp;
+  a.off_cnt = L.off_cnt;
   a.off_tacc = L.off_tacc;
   a.off_misc = L.off_misc;
   if (int(L.total) > di->max_smem_optin) return NS_ERR_INVALID_ARGUMENT;
