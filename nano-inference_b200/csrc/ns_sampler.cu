@@ -126,6 +126,7 @@ struct Misc {
   int g_ties;                   // this CTA's count of values equal to the top-p cut
   int g_tile;                   // inverse CDF: chosen tile of this CTA (-1: none)
   unsigned long long g_tbefore; // ... and the kept mass before it
+  int segoff[kWarps + 1];   // distinct history ids before each warp's columns
   int roff[kMaxLists + 1];  // leader: union offsets over (rank, warp) lists
   int rc0[kMaxCluster];     // leader: first column of each rank
   uint32_t hist[kBins];
@@ -154,10 +155,9 @@ struct KArgs {
   int per_warp;    // columns per warp (multiple of the 16-byte vector width)
   int tpw;         // tiles per warp (upper bound)
   int nwords;      // history bitmap words (one bit per column of a CTA)
-  int nsb;         // 256-column superblocks of the bitmap
-  int cnt_cap;     // distinct history ids the count array holds
+  int cnt_cap;     // distinct history ids the rank arrays hold
   int merge_cap;   // leader merge area (entries)
-  uint32_t off_bar, off_cand, off_bits, off_sbp, off_cnt, off_tacc, off_misc;
+  uint32_t off_bar, off_cand, off_bits, off_pre, off_cnt, off_colr, off_tacc, off_misc;
 };
 
 template <int DT>
@@ -172,8 +172,9 @@ struct Ctx {
   float* cx;  // [kWarps][kCapW]
   int* cid;   // [kWarps][kCapW]
   uint32_t* bits;  // history membership, one bit per CTA column
-  uint32_t* sbp;   // set bits before each 256-column superblock
-  int* cnt;        // occurrences of each distinct history id, by bit rank
+  uint16_t* pre;   // set bits of the owning warp's columns before each word
+  int* cnt;        // occurrences of each distinct history id, by rank
+  int* colr;       // CTA-relative column of each distinct history id, by rank
   void* tacc;
   Misc* m;
 
@@ -203,6 +204,9 @@ struct Ctx {
     return stages + (w * kWStages + s) * kWStageStride;
   }
   __device__ __forceinline__ uint64_t* sbar(int w, int s) const { return bar + w * kWStages + s; }
+  // Rank (distinct history ids before it, in column order) of CTA-relative
+  // column col, a multiple of 32 inside warp w's columns.
+  __device__ __forceinline__ int rank_at(int w, int col) const { return m->segoff[w] + pre[col >> 5]; }
 };
 
 // ---------------------------------------------------------------------------
@@ -435,67 +439,43 @@ __device__ void issue_tile(const Ctx<DT>& c, int w, int t, int s, uint64_t polic
   if (bytes) bulk_g2s(d + lead + head, src + head, bytes, c.sbar(w, s), policy);
 }
 
-// Penalise the history columns of warp tile (w, t).  Lane l reads the bitmap
-// words of tile columns [32 * (l + 32 k), +32); every set bit is a distinct
-// history id whose occurrence count is cnt[rank of the bit].  The penalised
-// value (negated when T < 0) goes to emit(has, x, col) -- called by all 32
-// lanes once per round, `has` false for lanes without a value, col relative
-// to the CTA's first column -- and the shared-memory slot becomes -inf so the
-// tile's own pass skips it.
+// Penalise the history columns of warp tile (w, t).  The prologue stored each
+// distinct history column of the CTA at its rank (history columns before it)
+// in colr[] and its occurrence count in cnt[]; ranks follow column order, so
+// the tile's history columns are the rank range [r0, r1).  Each penalised value
+// (negated when T < 0) goes to emit(has, x, col) -- called by all 32 lanes once
+// per round of 32 entries, `has` false for idle lanes, col relative to the
+// CTA's first column -- and its shared-memory slot becomes -inf so the tile's
+// own pass skips it.
 template <int DT, class Emit>
 __device__ __forceinline__ void patch_tile(const Ctx<DT>& c, int w, int t, uint8_t* st, float rep, float pres,
                                            float freq, Emit emit) {
   using E = Elem<DT>;
   using R = typename E::raw;
   constexpr int TE = Ctx<DT>::TE;
-  constexpr int WPL = TE / 32 / 32;  // bitmap words per lane per tile (1 or 2)
   if (!c.pen) return;
   const int lane = threadIdx.x & 31;
   const int base = w * c.pw + t * TE;  // a multiple of 32
-  const int len = c.tile_len(w, t), lead = c.tile_lead(w, t);
+  const int r0 = c.rank_at(w, base);
+  const int r1 = (t + 1 < c.wtiles(w)) ? c.rank_at(w, base + TE) : c.m->segoff[w + 1];
+  if (r1 <= r0) return;
+  const int lead = c.tile_lead(w, t);
   R* sr = reinterpret_cast<R*>(st);
-  uint32_t word[WPL], rem[WPL], rb[WPL];
-  bool any = false;
-#pragma unroll
-  for (int k = 0; k < WPL; ++k) {
-    const int off = (lane + 32 * k) * 32;  // tile column of the word's first bit
-    const int wi = (base + off) >> 5;
-    word[k] = (off < len && wi < c.nwords) ? c.bits[wi] : 0u;
-    rem[k] = word[k];
-    rb[k] = 0;
-    any |= word[k] != 0u;
-  }
-  if (!__any_sync(kFull, any)) return;
-#pragma unroll
-  for (int k = 0; k < WPL; ++k)
-    if (word[k]) {
-      const int wi = (base + (lane + 32 * k) * 32) >> 5;
-      uint32_t r = c.sbp[wi >> 3];
-      for (int j = wi & ~7; j < wi; ++j) r += __popc(c.bits[j]);
-      rb[k] = r;
-    }
-  while (true) {
-    bool has = false;
+  for (int r = r0; r < r1; r += 32) {
+    const int ri = r + lane;
+    const bool has = ri < r1;
     float xp = 0.0f;
     int col = 0;
-#pragma unroll
-    for (int k = 0; k < WPL; ++k)
-      if (!has && rem[k]) {
-        const int b = __ffs(rem[k]) - 1;
-        const int off = (lane + 32 * k) * 32 + b;
-        col = base + off;
-        const int e = lead + off;
-        const int count = c.cnt[rb[k] + __popc(word[k] & ((1u << b) - 1u))];
-        xp = penalize(E::widen(sr[e]), count, rep, pres, freq);
-        if (c.neg) xp = -xp;
-        sr[e] = c.neg ? E::pinf : E::ninf;
-        rem[k] &= rem[k] - 1u;
-        has = true;
-      }
-    if (!__any_sync(kFull, has)) break;
+    if (has) {
+      col = c.colr[ri];
+      const int e = lead + (col - base);
+      xp = penalize(E::widen(sr[e]), c.cnt[ri], rep, pres, freq);
+      if (c.neg) xp = -xp;
+      sr[e] = c.neg ? E::pinf : E::ninf;
+    }
     emit(has, xp, col);
   }
-  fence_proxy_async_smem();  // the slot is rewritten by a later bulk copy
+  fence_proxy_async_smem();  // the slots are rewritten by a later bulk copy
 }
 
 // ---------------------------------------------------------------------------
@@ -1729,7 +1709,6 @@ __device__ void general_row(const Ctx<DT>& c, const KArgs& a, cg::cluster_group&
 template <int DT>
 __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_constant__ KArgs a) {
   using C_ = Ctx<DT>;
-  constexpr int TE = C_::TE;
   extern __shared__ __align__(128) uint8_t smem[];
   cg::cluster_group cluster = cg::this_cluster();
   const int CL = int(cluster.num_blocks());
@@ -1743,8 +1722,9 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
   c.cx = reinterpret_cast<float*>(smem + a.off_cand);
   c.cid = reinterpret_cast<int*>(smem + a.off_cand + kWarps * kCapW * 4);
   c.bits = reinterpret_cast<uint32_t*>(smem + a.off_bits);
-  c.sbp = reinterpret_cast<uint32_t*>(smem + a.off_sbp);
+  c.pre = reinterpret_cast<uint16_t*>(smem + a.off_pre);
   c.cnt = reinterpret_cast<int*>(smem + a.off_cnt);
+  c.colr = reinterpret_cast<int*>(smem + a.off_colr);
   c.nwords = a.nwords;
   c.tacc = smem + a.off_tacc;
   c.m = reinterpret_cast<Misc*>(smem + a.off_misc);
@@ -1773,13 +1753,25 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
   }
   const bool pen = (h1 > h0) && (rep != 1.0f || pres != 0.0f || freq != 0.0f);
   c.pen = pen;
+  // The first kHB * kThreads history ids are loaded before any tile copy is
+  // queued, and stay in registers for both prologue passes.
+  constexpr int kHB = 8;
+  int ids0[kHB];
+  unsigned ids0_ok = 0;
+  if (pen) {
+#pragma unroll
+    for (int q = 0; q < kHB; ++q) {
+      const int64_t i = h0 + int64_t(q) * kThreads + tid;
+      ids0[q] = (i < h1) ? a.hist_ids[i] : 0;
+      ids0_ok |= (i < h1 ? 1u : 0u) << q;
+    }
+  }
   c.rowp = reinterpret_cast<const uint8_t*>(a.logits) + size_t(row) * size_t(a.row_stride) * C_::ES;
   c.row = row;
   c.c0 = int(min(int64_t(rank) * a.per_cta, a.vocab));
   c.c1 = int(min(int64_t(c.c0) + a.per_cta, a.vocab));
   c.pw = a.per_warp;
   c.tpw = a.tpw;
-  const int n_tiles_all = kWarps * a.tpw;
 
   if (tid == 0) {
     for (int s = 0; s < kWarps * kWStages; ++s) mbar_init(&c.bar[s], 1);
@@ -1804,23 +1796,26 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     for (int t = 0; t < min(kWStages, nt); ++t) issue_tile(c, warp, t, t, policy);
   }
 
-  // ---- history: membership bitmap and occurrence counts ----
-  // Fire-and-forget shared atomics only: bits are set with atomicOr, the
-  // prefix popcount of every 256-column superblock gives each distinct id a
-  // rank, and the counts are accumulated with atomicAdd at that rank.
+  // ---- history: membership bitmap, ranks and occurrence counts ----
+  // Fire-and-forget shared atomics only: bits are set with atomicOr; each warp
+  // scans the popcounts of its own columns' words (16-bit prefixes, the warp
+  // totals in segoff), which gives every distinct id a rank in column order;
+  // the counts are accumulated with atomicAdd at that rank.
   if (pen) {
-    constexpr int kHB = 8;  // ids loaded per thread per round trip
     auto for_ids = [&](auto f) {
-      for (int64_t base = h0; base < h1; base += int64_t(kThreads) * kHB) {
+#pragma unroll
+      for (int q = 0; q < kHB; ++q)
+        if ((ids0_ok >> q) & 1u) f(ids0[q]);
+      for (int64_t base = h0 + int64_t(kThreads) * kHB; base < h1; base += int64_t(kThreads) * kHB) {
         int ids[kHB];
 #pragma unroll
         for (int q = 0; q < kHB; ++q) {
           const int64_t i = base + int64_t(q) * kThreads + tid;
-          ids[q] = (i < h1) ? a.hist_ids[i] : INT_MIN;
+          ids[q] = (i < h1) ? a.hist_ids[i] : 0;
         }
 #pragma unroll
         for (int q = 0; q < kHB; ++q)
-          if (ids[q] != INT_MIN) f(ids[q]);
+          if (base + int64_t(q) * kThreads + tid < h1) f(ids[q]);
       }
     };
     for_ids([&](int id) {
@@ -1835,46 +1830,61 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
       }
     });
     __syncthreads();
-    {  // exclusive prefix popcount per superblock (contiguous chunks per thread)
-      const int per = (a.nsb + kThreads - 1) / kThreads;
-      const int s0 = min(tid * per, a.nsb), s1 = min(s0 + per, a.nsb);
-      uint32_t local = 0;
-      for (int sb = s0; sb < s1; ++sb)
-        for (int j = sb * 8; j < min(sb * 8 + 8, a.nwords); ++j) local += __popc(c.bits[j]);
-      uint32_t incl = local;
+    {  // this warp's words: 4 per lane per step, 16-byte loads
+      const int wpw = c.pw >> 5;  // a multiple of 4
+      const uint32_t* wb = c.bits + warp * wpw;
+      uint16_t* wp = c.pre + warp * wpw;
+      uint32_t run = 0;
+      for (int j0 = 0; j0 < wpw; j0 += 128) {
+        const int j = j0 + 4 * lane;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (j < wpw) v = *reinterpret_cast<const uint4*>(wb + j);
+        const uint32_t p0 = __popc(v.x), p1 = __popc(v.y), p2 = __popc(v.z), p3 = __popc(v.w);
+        const uint32_t sum = p0 + p1 + p2 + p3;
+        uint32_t incl = sum;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t v = __shfl_up_sync(kFull, incl, o);
-        if (lane >= o) incl += v;
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t u = __shfl_up_sync(kFull, incl, o);
+          if (lane >= o) incl += u;
+        }
+        const uint32_t e0 = run + incl - sum;
+        if (j < wpw) {
+          const uint32_t e1 = e0 + p0, e2 = e1 + p1, e3 = e2 + p2;
+          *reinterpret_cast<uint2*>(wp + j) = make_uint2((e0 & 0xFFFFu) | (e1 << 16), (e2 & 0xFFFFu) | (e3 << 16));
+        }
+        run += __shfl_sync(kFull, incl, 31);
       }
-      if (lane == 31) m->i_red[warp] = int(incl);
-      __syncthreads();
-      uint32_t run = incl - local, total = 0;
+      if (lane == 0) m->i_red[warp] = int(run);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int acc = 0;
+      bool wide = false;
       for (int w = 0; w < kWarps; ++w) {
-        if (w < warp) run += uint32_t(m->i_red[w]);
-        total += uint32_t(m->i_red[w]);
+        m->segoff[w] = acc;
+        acc += m->i_red[w];
+        wide |= m->i_red[w] > 0xFFFF;  // the 16-bit prefixes would wrap
       }
-      for (int sb = s0; sb < s1; ++sb) {
-        c.sbp[sb] = run;
-        for (int j = sb * 8; j < min(sb * 8 + 8, a.nwords); ++j) run += __popc(c.bits[j]);
-      }
-      if (total > uint32_t(a.cnt_cap) && tid == 0) atomicOr(&m->flags, F_HIST);
+      m->segoff[kWarps] = acc;
+      if (acc > a.cnt_cap || wide) atomicOr(&m->flags, F_HIST);
     }
     __syncthreads();
     if (!(m->flags & F_HIST)) {
+      const int wpw = c.pw >> 5;
       for_ids([&](int id) {
         const int64_t lc = int64_t(id) - a.vocab_offset;
         if (id >= 0 && lc >= c.c0 && lc < c.c1) {
           const int rel = int(lc - c.c0);
           const int wi = rel >> 5, b = rel & 31;
-          uint32_t r = c.sbp[wi >> 3];
-          for (int j = wi & ~7; j < wi; ++j) r += __popc(c.bits[j]);
-          r += __popc(c.bits[wi] & ((1u << b) - 1u));
+          const int r = m->segoff[wi / wpw] + c.pre[wi] + __popc(c.bits[wi] & ((1u << b) - 1u));
           atomicAdd(&c.cnt[r], 1);
+          c.colr[r] = rel;
         }
       });
     }
     __syncthreads();
+    // without ranks nothing may be patched (the row reports F_HIST)
+    if (m->flags & F_HIST) c.pen = false;
   }
 
   // ---- stream: every warp independently ----
@@ -2041,24 +2051,30 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
 // host side
 // ---------------------------------------------------------------------------
 struct Layout {
-  uint32_t off_bar, off_cand, off_bits, off_sbp, off_cnt, off_tacc, off_misc, total;
+  uint32_t off_bar, off_cand, off_bits, off_pre, off_cnt, off_colr, off_tacc, off_misc, total;
 };
 
 static uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
-static Layout make_layout(int nwords, int nsb, int cnt_cap, int n_tiles_all) {
+static Layout make_layout(int nwords, int cnt_cap, int n_tiles_all) {
   Layout L;
   uint32_t o = kStageBytes;
   L.off_bar = o;
   o += kWarps * kWStages * 8;
   o = align_up(o, 16);
-  L.off_cand = o;  // FAST candidate buffers / GENERAL histograms / tile expansion
-  o += kCandBytes;
+  // FAST candidate buffers / GENERAL histograms / tile expansion; during the
+  // history prologue (before any of those) the same bytes hold the bitmap,
+  // 16-byte aligned so every warp's words start on 16 bytes.
+  L.off_cand = o;
   L.off_bits = o;
-  o += uint32_t(nwords) * 4;
-  L.off_sbp = o;
-  o += uint32_t(nsb + 1) * 4;
+  o += std::max<uint32_t>(uint32_t(kCandBytes), uint32_t(nwords) * 4);
+  o = align_up(o, 16);
+  L.off_pre = o;
+  o += uint32_t(nwords) * 2;
+  o = align_up(o, 16);
   L.off_cnt = o;
+  o += uint32_t(cnt_cap) * 4;
+  L.off_colr = o;
   o += uint32_t(cnt_cap) * 4;
   o = align_up(o, 16);
   L.off_tacc = o;  // GENERAL: per-(warp, tile) mass (fixed point) and tie count
@@ -2103,23 +2119,23 @@ static int launch(const KArgs& base, int64_t batch, ns_stream_t stream) {
   int64_t per = (V + CL - 1) / CL;
   per = (per + C_::VE - 1) / C_::VE * C_::VE;
   int64_t pw = (per + kWarps - 1) / kWarps;
-  pw = (pw + 31) / 32 * 32;  // warp ranges start on bitmap words
+  pw = (pw + 127) / 128 * 128;  // warp ranges start on 16-byte groups of bitmap words
   a.per_cta = int(per);
   a.per_warp = int(pw);
   a.tpw = int((pw + C_::TE - 1) / C_::TE);
   const int n_tiles_all = kWarps * a.tpw;
   const int64_t span = int64_t(kWarps) * pw;  // columns one CTA may own
   a.nwords = a.hist_ids ? int((span + 31) / 32) : 0;
-  a.nsb = (a.nwords + 7) / 8;
   a.cnt_cap = a.hist_ids ? int(std::min<int64_t>(std::max<int64_t>(a.max_history, 1), span)) : 0;
-  const Layout L = make_layout(a.nwords, a.nsb, a.cnt_cap, n_tiles_all);
+  const Layout L = make_layout(a.nwords, a.cnt_cap, n_tiles_all);
   a.merge_cap = 1;
   while (a.merge_cap * 2 * 16 <= kStageBytes) a.merge_cap <<= 1;
   a.off_bar = L.off_bar;
   a.off_cand = L.off_cand;
   a.off_bits = L.off_bits;
-  a.off_sbp = L.off_sbp;
+  a.off_pre = L.off_pre;
   a.off_cnt = L.off_cnt;
+  a.off_colr = L.off_colr;
   a.off_tacc = L.off_tacc;
   a.off_misc = L.off_misc;
   if (int(L.total) > di->max_smem_optin) return NS_ERR_INVALID_ARGUMENT;
