@@ -143,6 +143,13 @@ __device__ __forceinline__ float fmax_nan(float a, float b) {
   return d;
 }
 
+// min that propagates NaN (PTX min.NaN, sm_80+).
+__device__ __forceinline__ float fmin_nan(float a, float b) {
+  float d;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+
 __device__ __forceinline__ uint32_t lanemask_lt() {
   uint32_t m;
   asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));

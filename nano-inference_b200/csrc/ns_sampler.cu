@@ -42,6 +42,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <type_traits>
 #include <climits>
 #include <cstdint>
 #include <cstring>
@@ -66,7 +67,6 @@ constexpr int kFastK = 128;                     // largest top_k served by the s
 constexpr int kCandBytes = kWarps * kCapW * 8;  // candidate buffers (x, col)
 constexpr int kBins = 256;                      // radix digit = 8 bits (one bin per thread)
 static_assert(kBins == kThreads, "block_kth_regs clears one bin per thread");
-constexpr int kRefreshTile = 3;                 // FAST: CTA-wide threshold refresh after this warp tile
 constexpr int kMaxCluster = 8;
 constexpr int kMaxLists = kMaxCluster * kWarps;
 constexpr unsigned kFull = 0xFFFFFFFFu;
@@ -127,6 +127,7 @@ struct Misc {
   int g_tile;                   // inverse CDF: chosen tile of this CTA (-1: none)
   unsigned long long g_tbefore; // ... and the kept mass before it
   int segoff[kWarps + 1];   // distinct history ids before each warp's columns
+  uint32_t pub[kWarps];     // FAST: per-warp published bound (key; 0 = none)
   int roff[kMaxLists + 1];  // leader: union offsets over (rank, warp) lists
   int rc0[kMaxCluster];     // leader: first column of each rank
   uint32_t hist[kBins];
@@ -157,7 +158,7 @@ struct KArgs {
   int nwords;      // history bitmap words (one bit per column of a CTA)
   int cnt_cap;     // distinct history ids the rank arrays hold
   int merge_cap;   // leader merge area (entries)
-  uint32_t off_bar, off_cand, off_bits, off_pre, off_cnt, off_colr, off_tacc, off_misc;
+  uint32_t off_bar, off_cand, off_bits, off_pre, off_cnt, off_colr, off_pval, off_tacc, off_misc;
 };
 
 template <int DT>
@@ -175,6 +176,7 @@ struct Ctx {
   uint16_t* pre;   // set bits of the owning warp's columns before each word
   int* cnt;        // occurrences of each distinct history id, by rank
   int* colr;       // CTA-relative column of each distinct history id, by rank
+  float* pval;     // its penalised value (negated when T < 0), by rank
   void* tacc;
   Misc* m;
 
@@ -187,6 +189,7 @@ struct Ctx {
   bool neg;
   bool pen;  // this row has a history and a non-neutral penalty
   float Tabs;
+  float rep, pres, freq;
 
   __device__ __forceinline__ int w0(int w) const { return min(c0 + w * pw, c1); }
   __device__ __forceinline__ int w1(int w) const { return min(c0 + (w + 1) * pw, c1); }
@@ -439,43 +442,57 @@ __device__ void issue_tile(const Ctx<DT>& c, int w, int t, int s, uint64_t polic
   if (bytes) bulk_g2s(d + lead + head, src + head, bytes, c.sbar(w, s), policy);
 }
 
-// Penalise the history columns of warp tile (w, t).  The prologue stored each
-// distinct history column of the CTA at its rank (history columns before it)
-// in colr[] and its occurrence count in cnt[]; ranks follow column order, so
-// the tile's history columns are the rank range [r0, r1).  Each penalised value
-// (negated when T < 0) goes to emit(has, x, col) -- called by all 32 lanes once
-// per round of 32 entries, `has` false for idle lanes, col relative to the
-// CTA's first column -- and its shared-memory slot becomes -inf so the tile's
-// own pass skips it.
-template <int DT, class Emit>
-__device__ __forceinline__ void patch_tile(const Ctx<DT>& c, int w, int t, uint8_t* st, float rep, float pres,
-                                           float freq, Emit emit) {
-  using E = Elem<DT>;
-  using R = typename E::raw;
+// History columns of warp tile (w, t).  The prologue stored each distinct
+// history column of the CTA at its rank (history columns before it): colr[]
+// its CTA-relative column, pval[] its penalised value (negated when T < 0).
+// Ranks follow column order, so a tile's history columns are one rank range.
+template <int DT>
+__device__ __forceinline__ int2 tile_ranks(const Ctx<DT>& c, int w, int t) {
   constexpr int TE = Ctx<DT>::TE;
-  if (!c.pen) return;
-  const int lane = threadIdx.x & 31;
   const int base = w * c.pw + t * TE;  // a multiple of 32
   const int r0 = c.rank_at(w, base);
   const int r1 = (t + 1 < c.wtiles(w)) ? c.rank_at(w, base + TE) : c.m->segoff[w + 1];
-  if (r1 <= r0) return;
+  return make_int2(r0, r1);
+}
+
+// Penalise the history columns of a landed tile: each value is computed from
+// its slot and its occurrence count, stored at its rank in pval[] and passed
+// to emit(has, x, col) -- called by all 32 lanes once per round of 32
+// entries, `has` false for idle lanes, col relative to the CTA's first column
+// -- and the slot becomes -inf so passes over the raw slots skip it.
+template <int DT, class Emit>
+__device__ __forceinline__ void patch_tile(const Ctx<DT>& c, int w, int t, uint8_t* st, Emit emit) {
+  using E = Elem<DT>;
+  using R = typename E::raw;
+  if (!c.pen) return;
+  const int lane = threadIdx.x & 31;
+  const int2 rr = tile_ranks(c, w, t);
+  if (rr.y <= rr.x) return;
+  const int base = w * c.pw + t * Ctx<DT>::TE;
   const int lead = c.tile_lead(w, t);
   R* sr = reinterpret_cast<R*>(st);
-  for (int r = r0; r < r1; r += 32) {
+  for (int r = rr.x; r < rr.y; r += 32) {
     const int ri = r + lane;
-    const bool has = ri < r1;
+    const bool has = ri < rr.y;
     float xp = 0.0f;
     int col = 0;
     if (has) {
       col = c.colr[ri];
       const int e = lead + (col - base);
-      xp = penalize(E::widen(sr[e]), c.cnt[ri], rep, pres, freq);
+      xp = penalize(E::widen(sr[e]), c.cnt[ri], c.rep, c.pres, c.freq);
       if (c.neg) xp = -xp;
+      c.pval[ri] = xp;
       sr[e] = c.neg ? E::pinf : E::ninf;
     }
     emit(has, xp, col);
   }
   fence_proxy_async_smem();  // the slots are rewritten by a later bulk copy
+}
+
+// Penalise without emitting (the values are taken from pval[] later).
+template <int DT>
+__device__ __forceinline__ void mask_tile(const Ctx<DT>& c, int w, int t, uint8_t* st) {
+  patch_tile(c, w, t, st, [](bool, float, int) {});
 }
 
 // ---------------------------------------------------------------------------
@@ -565,6 +582,101 @@ __device__ __forceinline__ void group_append(const Ctx<DT>& c, WarpCand& s, int 
   s.n += __popc(mk);
 }
 
+// ---------------------------------------------------------------------------
+// full tiles (every slot a column, first column 16-byte aligned): lane l holds
+// 16-byte groups l, l + 32, ... in registers; one NaN-propagating max per lane
+// decides whether any element needs a closer look
+// ---------------------------------------------------------------------------
+template <int DT>
+constexpr int kGroupsPerLane = Ctx<DT>::TE / Ctx<DT>::VE / 32;
+
+// Largest value of one 16-byte group in the filter domain (negated when NEG):
+// NaN if any is NaN.  16-bit types reduce pairwise in their own format, which
+// is exact (max is a selection).
+template <int DT, bool NEG>
+__device__ __forceinline__ float group_extreme(const uint4& v) {
+  if constexpr (DT == NS_DTYPE_F32) {
+    const float x0 = __uint_as_float(v.x), x1 = __uint_as_float(v.y);
+    const float x2 = __uint_as_float(v.z), x3 = __uint_as_float(v.w);
+    return NEG ? -fmin_nan(fmin_nan(x0, x1), fmin_nan(x2, x3)) : fmax_nan(fmax_nan(x0, x1), fmax_nan(x2, x3));
+  } else {
+    using P = typename std::conditional<DT == NS_DTYPE_BF16, __nv_bfloat162, __half2>::type;
+    auto as2 = [](uint32_t u) {
+      P p;
+      memcpy(&p, &u, 4);
+      return p;
+    };
+    auto op = [](P x, P y) { return NEG ? __hmin2_nan(x, y) : __hmax2_nan(x, y); };
+    const P a = op(op(as2(v.x), as2(v.y)), op(as2(v.z), as2(v.w)));
+    uint32_t u;
+    memcpy(&u, &a, 4);
+    const float lo = Elem<DT>::widen(uint16_t(u & 0xFFFFu)), hi = Elem<DT>::widen(uint16_t(u >> 16));
+    return NEG ? -fmin_nan(lo, hi) : fmax_nan(lo, hi);
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ void load_full(const uint8_t* st, uint4 (&v)[kGroupsPerLane<DT>]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < kGroupsPerLane<DT>; ++k) v[k] = *reinterpret_cast<const uint4*>(st + (k * 32 + lane) * 16);
+}
+
+// FAST filter of a full tile: a per-lane mask of the groups whose max reaches
+// tau (or is NaN) and one vote; hot groups are re-read from shared memory one
+// per lane per round (lanes may work on different groups in one round).
+template <int DT, bool NEG>
+__device__ __forceinline__ void fast_full(const Ctx<DT>& c, WarpCand& s, const uint8_t* st, int colbase) {
+  constexpr int VE = Ctx<DT>::VE, TE = Ctx<DT>::TE, G = kGroupsPerLane<DT>;
+  const int lane = threadIdx.x & 31;
+  unsigned gm = 0;
+  {
+    uint4 v[G];
+    load_full<DT>(st, v);
+#pragma unroll
+    for (int k = 0; k < G; ++k) gm |= (group_extreme<DT, NEG>(v[k]) < s.tau ? 0u : 1u) << k;
+  }
+  while (__any_sync(kFull, gm != 0u)) {
+    const bool h = gm != 0u;
+    const int k = h ? __ffs(gm) - 1 : 0;
+    gm &= gm - 1u;
+    float x[VE];
+    unpack16<DT>(*reinterpret_cast<const uint4*>(st + (k * 32 + lane) * 16), x);
+    bool cold = true;
+#pragma unroll
+    for (int i = 0; i < VE; ++i) {
+      if (NEG) x[i] = -x[i];
+      cold = cold && (x[i] < s.tau);  // tau may have risen in this tile
+    }
+    const bool hh = h && !cold;
+    if (__any_sync(kFull, hh)) group_append(c, s, k * 32 + lane, x, hh, 0, TE, TE / VE, colbase);
+  }
+}
+
+// GREEDY of a full tile: per-lane running argmax under the full (value, first
+// index, NaN first) order; groups whose max cannot win are skipped.
+template <int DT>
+__device__ __forceinline__ void greedy_full(const uint8_t* st, int colbase, float& best, int& bidx) {
+  constexpr int VE = Ctx<DT>::VE, G = kGroupsPerLane<DT>;
+  const int lane = threadIdx.x & 31;
+  uint4 v[G];
+  load_full<DT>(st, v);
+#pragma unroll
+  for (int k = 0; k < G; ++k) {
+    if (group_extreme<DT, false>(v[k]) <= best && bidx != INT_MAX) continue;
+    float x[VE];
+    unpack16<DT>(v[k], x);
+#pragma unroll
+    for (int i = 0; i < VE; ++i) {
+      const int col = colbase + (k * 32 + lane) * VE + i;
+      if (better(x[i], col, best, bidx)) {
+        best = x[i];
+        bidx = col;
+      }
+    }
+  }
+}
+
 // FAST filter of one landed tile: two 16-byte groups per lane per step, each
 // with its own vote; the common group is a shared load, a compare chain and
 // a vote.
@@ -575,6 +687,10 @@ __device__ __forceinline__ void fast_tile(const Ctx<DT>& c, WarpCand& s, int w, 
   const int len = c.tile_len(w, t), lead = c.tile_lead(w, t);
   const int n_groups = (lead + len + VE - 1) / VE;
   const int colbase = w * c.pw + t * TE - lead;  // CTA-relative column of slot 0
+  if (len == TE && lead == 0) {
+    fast_full<DT, NEG>(c, s, st, colbase);
+    return;
+  }
   for (int q0 = 0; q0 < n_groups; q0 += 64) {
     const int qa = q0 + lane, qb = q0 + 32 + lane;
     float xa[VE], xb[VE];
@@ -600,10 +716,9 @@ __device__ __forceinline__ void fast_emit(const Ctx<DT>& c, WarpCand& s, bool ha
   warp_append_bits(c, s, (has && !bad && xp >= s.tau && xp > -INFINITY) ? 1u : 0u, v, col);
 }
 
-// GREEDY of one landed tile: per-lane running first-index argmax.  A lane sees
-// its slots in increasing column order, so a strict '>' keeps the first
-// index; a NaN-propagating group max skips groups that cannot win.  Bucket
-// entries arrive out of order and use the full comparison.
+// GREEDY of one landed tile: per-lane running argmax under the full (value,
+// first index, NaN first) order; the penalised history values arrive out of
+// column order.  A group whose NaN-propagating max cannot win is skipped.
 template <int DT>
 __device__ __forceinline__ void greedy_group(const float (&x)[Ctx<DT>::VE], int q, int lead, int len, int n_groups,
                                              int colbase, float& best, int& bidx) {
@@ -611,15 +726,14 @@ __device__ __forceinline__ void greedy_group(const float (&x)[Ctx<DT>::VE], int 
   float m = x[0];
 #pragma unroll
   for (int i = 1; i < VE; ++i) m = fmax_nan(m, x[i]);
-  if (!(m <= best) || bidx == INT_MAX) {
+  if (m <= best && bidx != INT_MAX) return;
 #pragma unroll
-    for (int i = 0; i < VE; ++i) {
-      const int e = q * VE + i;
-      const bool valid = (q < n_groups) && e >= lead && e < lead + len;
-      if (valid && (bidx == INT_MAX || x[i] > best || (x[i] != x[i] && best == best))) {
-        best = x[i];
-        bidx = colbase + e;
-      }
+  for (int i = 0; i < VE; ++i) {
+    const int e = q * VE + i;
+    const bool valid = (q < n_groups) && e >= lead && e < lead + len;
+    if (valid && better(x[i], colbase + e, best, bidx)) {
+      best = x[i];
+      bidx = colbase + e;
     }
   }
 }
@@ -632,28 +746,147 @@ __device__ __forceinline__ void greedy_tile(const Ctx<DT>& c, int w, int t, cons
   const int len = c.tile_len(w, t), lead = c.tile_lead(w, t);
   const int n_groups = (lead + len + VE - 1) / VE;
   const int colbase = c.c0 + w * c.pw + t * TE - lead;  // call-local column of slot 0
-  if (best == best) {  // a lane that has seen a NaN keeps its first NaN
-    for (int q0 = 0; q0 < n_groups; q0 += 64) {
-      const int qa = q0 + lane, qb = q0 + 32 + lane;
-      float xa[VE], xb[VE];
-      load_group<DT, false>(st, qa, n_groups, xa);
-      load_group<DT, false>(st, qb, n_groups, xb);
-      greedy_group<DT>(xa, qa, lead, len, n_groups, colbase, best, bidx);
-      greedy_group<DT>(xb, qb, lead, len, n_groups, colbase, best, bidx);
-    }
+  if (len == TE && lead == 0) {
+    greedy_full<DT>(st, colbase, best, bidx);
+    return;
+  }
+  for (int q0 = 0; q0 < n_groups; q0 += 64) {
+    const int qa = q0 + lane, qb = q0 + 32 + lane;
+    float xa[VE], xb[VE];
+    load_group<DT, false>(st, qa, n_groups, xa);
+    load_group<DT, false>(st, qb, n_groups, xb);
+    greedy_group<DT>(xa, qa, lead, len, n_groups, colbase, best, bidx);
+    greedy_group<DT>(xb, qb, lead, len, n_groups, colbase, best, bidx);
   }
 }
 
-// Stream tiles [t_begin, t_end) of this warp's columns (its first kWStages
-// copies were issued before the history prologue; tiles below n_ready were
-// already waited for and patched).  mode: GREEDY or FAST.  Returns false if a
-// bounded wait gave up (F_TIMEOUT is set); in-flight copies are drained first.
+// Largest finite value of the lane's slots of a landed tile in the filter
+// domain (-inf if none; a lane holding a NaN or +inf contributes nothing).
+template <int DT, bool NEG>
+__device__ __forceinline__ float tile_lane_max(const Ctx<DT>& c, int w, int t, const uint8_t* st) {
+  constexpr int VE = Ctx<DT>::VE, TE = Ctx<DT>::TE;
+  const int lane = threadIdx.x & 31;
+  const int len = c.tile_len(w, t), lead = c.tile_lead(w, t);
+  if (len == TE && lead == 0) {
+    uint4 v[kGroupsPerLane<DT>];
+    load_full<DT>(st, v);
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < kGroupsPerLane<DT>; ++k) {
+      const float g = group_extreme<DT, NEG>(v[k]);
+      if (g > -INFINITY && g < INFINITY) m = fmaxf(m, g);  // a group holding NaN or +inf is left out
+    }
+    return m;
+  }
+  const int n_groups = (lead + len + VE - 1) / VE;
+  float tmax = -INFINITY;
+  for (int q = lane; q < n_groups; q += 32) {
+    float x[VE];
+    unpack16<DT>(*reinterpret_cast<const uint4*>(st + q * 16), x);
+#pragma unroll
+    for (int i = 0; i < VE; ++i) {
+      const int e = q * VE + i;
+      const float xk = NEG ? -x[i] : x[i];
+      if (e >= lead && e < lead + len && xk > -INFINITY && xk < INFINITY) tmax = fmaxf(tmax, xk);
+    }
+  }
+  return tmax;
+}
+
+// ---------------------------------------------------------------------------
+// FAST threshold sharing without block barriers.  A warp publishes a bound
+// from v_w, the kq-th largest (kq = ceil(K / kWarps)) element it holds; every
+// element of the warp's columns >= its own tau is held, so v_w has kq elements
+// of the CTA at or above it.  Once all kWarps warps have published, the CTA has
+// at least kWarps * kq >= K elements >= min_w v_w: a lower bound of its K-th
+// largest.  The published value is already the collision-safe filter bound
+// scaled_lower_bound(v_w), which is monotone in v_w, so the minimum of the
+// published bounds is the bound of min_w v_w.  Published values only grow, so
+// a stale read is still valid.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int share_kq(int K) { return (K + kWarps - 1) / kWarps; }
+
+// kq-th largest (with multiplicity) of one key per lane; 0 if fewer than kq
+// non-zero keys.
+__device__ __forceinline__ uint32_t warp_kth_lanes(uint32_t key, int kq) {
+  const int lane = threadIdx.x & 31;
+  uint32_t res = 0;
+  for (int j = 0; j < kq; ++j) {
+    res = __reduce_max_sync(kFull, key);
+    if (res == 0u) break;
+    const unsigned b = __ballot_sync(kFull, key == res);
+    if (lane == __ffs(b) - 1) key = 0u;
+  }
+  return res;
+}
+
+// kq-th largest (with multiplicity) of the warp's buffer; 0 if fewer entries.
+__device__ __forceinline__ uint32_t warp_kth_buffer(const WarpCand& s, int kq) {
+  const int lane = threadIdx.x & 31;
+  if (s.n < kq) return 0u;
+  uint32_t key[kPerLane];
+#pragma unroll
+  for (int q = 0; q < kPerLane; ++q) {
+    const int i = q * 32 + lane;
+    key[q] = (i < s.n) ? f2key(s.x[i]) : 0u;
+  }
+  uint32_t res = 0;
+  for (int j = 0; j < kq; ++j) {
+    uint32_t lm = key[0];
+#pragma unroll
+    for (int q = 1; q < kPerLane; ++q) lm = max(lm, key[q]);
+    res = __reduce_max_sync(kFull, lm);
+    const unsigned b = __ballot_sync(kFull, lm == res);
+    if (lane == __ffs(b) - 1) {
+      bool done = false;
+#pragma unroll
+      for (int q = 0; q < kPerLane; ++q)
+        if (!done && key[q] == res) {
+          key[q] = 0u;
+          done = true;
+        }
+    }
+  }
+  return res;
+}
+
+// Raise tau to the shared bound (all lanes call).
 template <int DT>
-__device__ __forceinline__ bool stream_warp(const Ctx<DT>& c, int mode, uint64_t policy, float rep, float pres, float freq,
-                            int t_begin, int t_end, int n_ready, WarpCand& s, float& best, int& bidx) {
+__device__ __forceinline__ void read_shared_tau(const Ctx<DT>& c, WarpCand& s) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t p = (lane < kWarps) ? static_cast<volatile uint32_t*>(c.m->pub)[lane] : 0xFFFFFFFFu;
+  const uint32_t mn = __reduce_min_sync(kFull, p);
+  if (mn != 0u) s.tau = fmaxf(s.tau, key2f(mn));
+}
+
+// Publish this warp's bound from the kq-th largest value v (key; 0 = none).
+template <int DT>
+__device__ __forceinline__ void publish_key(const Ctx<DT>& c, uint32_t v) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0 && v != 0u) {
+    const uint32_t b = f2key(scaled_lower_bound(key2f(v), c.Tabs));
+    volatile uint32_t* pub = c.m->pub;
+    if (b > pub[warp]) pub[warp] = b;
+  }
+  __syncwarp();
+}
+
+template <int DT>
+__device__ __forceinline__ void publish_bound(const Ctx<DT>& c, const WarpCand& s) {
+  if (s.ovf) return;
+  publish_key(c, warp_kth_buffer(s, share_kq(c.K)));
+}
+
+// Stream this warp's tiles from t_begin (its first kWStages copies were issued
+// before the history prologue; tiles below n_ready were already waited for and
+// masked).  mode: GREEDY or FAST.  Returns false if a bounded wait gave up
+// (F_TIMEOUT is set); in-flight copies are drained first.
+template <int DT>
+__device__ __forceinline__ bool stream_warp(const Ctx<DT>& c, int mode, uint64_t policy, int t_begin, int n_ready,
+                                            WarpCand& s, float& best, int& bidx) {
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nt = c.wtiles(w);
-  for (int t = t_begin; t < min(nt, t_end); ++t) {
+  for (int t = t_begin; t < nt; ++t) {
     const int sidx = t % kWStages;
     uint8_t* st = c.stage(w, sidx);
     if (t >= n_ready) {
@@ -667,17 +900,10 @@ __device__ __forceinline__ bool stream_warp(const Ctx<DT>& c, int mode, uint64_t
         __syncwarp();
         return false;
       }
-      if (mode == MODE_GREEDY) {
-        patch_tile(c, w, t, st, rep, pres, freq, [&](bool has, float xp, int col) {
-          if (has && better(xp, c.c0 + col, best, bidx)) {
-            best = xp;
-            bidx = c.c0 + col;
-          }
-        });
-      } else if (!s.ovf) {
-        patch_tile(c, w, t, st, rep, pres, freq, [&](bool has, float xp, int col) { fast_emit(c, s, has, xp, col); });
+      if (c.pen) {
+        mask_tile(c, w, t, st);
+        __syncwarp();
       }
-      __syncwarp();
     }
     if (mode == MODE_GREEDY) {
       greedy_tile(c, w, t, st, best, bidx);
@@ -686,6 +912,8 @@ __device__ __forceinline__ bool stream_warp(const Ctx<DT>& c, int mode, uint64_t
         fast_tile<DT, true>(c, s, w, t, st);
       else
         fast_tile<DT, false>(c, s, w, t, st);
+      if ((t & 3) == 1) publish_bound(c, s);
+      read_shared_tau(c, s);
     }
     __syncwarp();
     if (lane == 0 && t + kWStages < nt) issue_tile(c, w, t + kWStages, (t + kWStages) % kWStages, policy);
@@ -1216,7 +1444,7 @@ __device__ __forceinline__ bool warp_pass(const Ctx<DT>& c, int& seq, int pre_is
       return false;
     }
     uint8_t* st = c.stage(w, sidx);
-    patch_tile(c, w, t, st, rep, pres, freq, [&](bool has, float xp, int col) {
+    patch_tile(c, w, t, st, [&](bool has, float xp, int col) {
       if (has) fe(xp, col);
     });
     __syncwarp();
@@ -1626,7 +1854,7 @@ __device__ void general_row(const Ctx<DT>& c, const KArgs& a, cg::cluster_group&
   }
   __syncwarp();
   // history columns get their penalised values on top of the raw ones
-  patch_tile(c, warp, t, st, rep, pres, freq, [&](bool has, float xp, int col) {
+  patch_tile(c, warp, t, st, [&](bool has, float xp, int col) {
     if (has) F[col - base] = xp;
   });
   __syncwarp();
@@ -1725,6 +1953,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
   c.pre = reinterpret_cast<uint16_t*>(smem + a.off_pre);
   c.cnt = reinterpret_cast<int*>(smem + a.off_cnt);
   c.colr = reinterpret_cast<int*>(smem + a.off_colr);
+  c.pval = reinterpret_cast<float*>(smem + a.off_pval);
   c.nwords = a.nwords;
   c.tacc = smem + a.off_tacc;
   c.m = reinterpret_cast<Misc*>(smem + a.off_misc);
@@ -1753,6 +1982,9 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
   }
   const bool pen = (h1 > h0) && (rep != 1.0f || pres != 0.0f || freq != 0.0f);
   c.pen = pen;
+  c.rep = rep;
+  c.pres = pres;
+  c.freq = freq;
   // The first kHB * kThreads history ids are loaded before any tile copy is
   // queued, and stay in registers for both prologue passes.
   constexpr int kHB = 8;
@@ -1781,6 +2013,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     m->choose = INT_MAX;
     m->g_best = -INFINITY;
     m->g_idx = INT_MAX;
+    for (int w = 0; w < kWarps; ++w) m->pub[w] = 0u;
   }
   if (pen) {
     for (int i = tid; i < a.nwords; i += kThreads) c.bits[i] = 0u;
@@ -1800,12 +2033,23 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
   // Fire-and-forget shared atomics only: bits are set with atomicOr; each warp
   // scans the popcounts of its own columns' words (16-bit prefixes, the warp
   // totals in segoff), which gives every distinct id a rank in column order;
-  // the counts are accumulated with atomicAdd at that rank.
+  // the counts are accumulated with atomicAdd at that rank.  The penalised
+  // values are computed when their tiles land (patch_tile).
   if (pen) {
-    auto for_ids = [&](auto f) {
 #pragma unroll
-      for (int q = 0; q < kHB; ++q)
-        if ((ids0_ok >> q) & 1u) f(ids0[q]);
+    for (int q = 0; q < kHB; ++q) {
+      if ((ids0_ok >> q) & 1u) {
+        const int id = ids0[q];
+        const int64_t lc = int64_t(id) - a.vocab_offset;
+        if (id < 0 || int64_t(id) >= a.vocab_total) {
+          atomicOr(&m->flags, F_BADID);
+        } else if (lc >= c.c0 && lc < c.c1) {
+          const int rel = int(lc - c.c0);
+          atomicOr(&c.bits[rel >> 5], 1u << (rel & 31));
+        }
+      }
+    }
+    auto for_more_ids = [&](auto f) {  // ids past the first kHB * kThreads
       for (int64_t base = h0 + int64_t(kThreads) * kHB; base < h1; base += int64_t(kThreads) * kHB) {
         int ids[kHB];
 #pragma unroll
@@ -1818,7 +2062,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
           if (base + int64_t(q) * kThreads + tid < h1) f(ids[q]);
       }
     };
-    for_ids([&](int id) {
+    for_more_ids([&](int id) {
       if (id < 0 || int64_t(id) >= a.vocab_total) {
         atomicOr(&m->flags, F_BADID);
         return;
@@ -1871,15 +2115,21 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     __syncthreads();
     if (!(m->flags & F_HIST)) {
       const int wpw = c.pw >> 5;
-      for_ids([&](int id) {
-        const int64_t lc = int64_t(id) - a.vocab_offset;
-        if (id >= 0 && lc >= c.c0 && lc < c.c1) {
-          const int rel = int(lc - c.c0);
-          const int wi = rel >> 5, b = rel & 31;
-          const int r = m->segoff[wi / wpw] + c.pre[wi] + __popc(c.bits[wi] & ((1u << b) - 1u));
-          atomicAdd(&c.cnt[r], 1);
-          c.colr[r] = rel;
+      auto count = [&](int rel) {
+        const int wi = rel >> 5, b = rel & 31;
+        const int r = m->segoff[wi / wpw] + c.pre[wi] + __popc(c.bits[wi] & ((1u << b) - 1u));
+        atomicAdd(&c.cnt[r], 1);
+        c.colr[r] = rel;
+      };
+#pragma unroll
+      for (int q = 0; q < kHB; ++q)
+        if ((ids0_ok >> q) & 1u) {
+          const int64_t lc = int64_t(ids0[q]) - a.vocab_offset;
+          if (ids0[q] >= 0 && lc >= c.c0 && lc < c.c1) count(int(lc - c.c0));
         }
+      for_more_ids([&](int id) {
+        const int64_t lc = int64_t(id) - a.vocab_offset;
+        if (id >= 0 && lc >= c.c0 && lc < c.c1) count(int(lc - c.c0));
       });
     }
     __syncthreads();
@@ -1898,72 +2148,60 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
   int bidx = INT_MAX;
   int n_ready = 0;
   if (mode == MODE_FAST) {
-    // Seed tau from a CTA-wide sample: the K-th largest of the 256 per-thread
-    // maxima over every warp's first kWStages tiles.  They are distinct
-    // elements of this CTA's columns, so their K-th largest is a lower bound
-    // of the CTA's K-th largest, and for K << 256 it is nearly as tight as
-    // the sample's own.
+    // Seed: each warp publishes the kq-th largest of its 32 lane maxima over
+    // its first kWStages tiles (distinct elements); after one block barrier
+    // every warp starts from the shared bound.
     float tmax = -INFINITY;
     const int nr = min(kWStages, c.wtiles(warp));
     bool ready = true;
     for (int t = 0; t < nr; ++t) ready = ready && __all_sync(kFull, mbar_wait_bounded(c.sbar(warp, t), 0u));
     if (ready) {
       n_ready = nr;
-      constexpr int VE = C_::VE;
       for (int t = 0; t < nr; ++t) {
         uint8_t* st = c.stage(warp, t);
-        patch_tile(c, warp, t, st, rep, pres, freq, [&](bool has, float xk, int col) {
-          if (has && xk > -INFINITY && xk < INFINITY) tmax = fmaxf(tmax, xk);
-          fast_emit(c, s, has, xk, col);
-        });
-        __syncwarp();
-        const int len = c.tile_len(warp, t), lead = c.tile_lead(warp, t);
-        const int n_groups = (lead + len + VE - 1) / VE;
-        for (int q = lane; q < n_groups; q += 32) {
-          float x[VE];
-          unpack16<DT>(*reinterpret_cast<const uint4*>(st + q * 16), x);
-#pragma unroll
-          for (int i = 0; i < VE; ++i) {
-            const int e = q * VE + i;
-            const float xk = c.neg ? -x[i] : x[i];
-            if (e >= lead && e < lead + len && xk > -INFINITY && xk < INFINITY) tmax = fmaxf(tmax, xk);
-          }
+        if (c.pen) {
+          mask_tile(c, warp, t, st);
+          __syncwarp();
         }
+        tmax = fmaxf(tmax, c.neg ? tile_lane_max<DT, true>(c, warp, t, st) : tile_lane_max<DT, false>(c, warp, t, st));
       }
     }
-    const uint32_t mk = (tmax > -INFINITY) ? f2key(tmax) : 0u;
-    if (__syncthreads_count(mk != 0u) >= c.K) {
-      uint32_t pre = 0;
-      for (int b = 31; b >= 0; --b) {
-        const uint32_t cand = pre | (1u << b);
-        if (__syncthreads_count(mk >= cand) >= c.K) pre = cand;
-      }
-      s.tau = scaled_lower_bound(key2f(pre), c.Tabs);
-    }
+    publish_key(c, warp_kth_lanes(tmax > -INFINITY ? f2key(tmax) : 0u, share_kq(c.K)));
+    __syncthreads();
+    read_shared_tau(c, s);
   }
   bool ok = true;
-  if (streams) {
-    if (mode == MODE_FAST && c.tpw >= 2 * (kRefreshTile + 1)) {
-      ok = stream_warp(c, mode, policy, rep, pres, freq, 0, kRefreshTile + 1, n_ready, s, best, bidx);
-      // CTA-wide refresh: the K-th largest over every warp's candidates so far
-      // is a lower bound of the CTA's K-th largest; all warps filter with it.
-      uint32_t key[kPerLane];
-#pragma unroll
-      for (int q = 0; q < kPerLane; ++q) {
-        const int i = q * 32 + lane;
-        key[q] = (i < s.n && !s.ovf) ? f2key(s.x[i]) : 0u;
+  if (streams) ok = stream_warp(c, mode, policy, 0, n_ready, s, best, bidx);
+  // this warp's penalised history values (computed as its tiles landed): the
+  // rank range of its columns
+  if (ok && c.pen) {
+    const int hr0 = m->segoff[warp], hr1 = m->segoff[warp + 1];
+    if (mode == MODE_GREEDY) {
+      for (int r = hr0 + lane; r < hr1; r += 32) {
+        const float x = c.pval[r];
+        const int col = c.c0 + c.colr[r];
+        if (better(x, col, best, bidx)) {
+          best = x;
+          bidx = col;
+        }
       }
-      uint32_t kk = 0;
-      if (block_kth_regs(m, key, c.K, &kk)) {
-        s.tau = fmaxf(s.tau, scaled_lower_bound(key2f(kk), c.Tabs));
-        if (!s.ovf) warp_drop_below(s);
+    } else if (mode == MODE_FAST && !s.ovf) {
+      for (int r0 = hr0; r0 < hr1; r0 += 32) {
+        const int r = r0 + lane;
+        const bool has = r < hr1;
+        fast_emit(c, s, has, has ? c.pval[r] : 0.0f, has ? c.colr[r] : 0);
       }
-      if (ok) ok = stream_warp(c, mode, policy, rep, pres, freq, kRefreshTile + 1, INT_MAX, n_ready, s, best, bidx);
-    } else {
-      ok = stream_warp(c, mode, policy, rep, pres, freq, 0, INT_MAX, n_ready, s, best, bidx);
     }
   }
   if (mode == MODE_FAST && s.ovf && lane == 0) atomicOr(&m->flags, F_OVF);
+  if (mode == MODE_FAST) {  // every warp's final bound; survivors of the tightest
+    if (ok) publish_bound(c, s);
+    __syncthreads();
+    if (!s.ovf) {
+      read_shared_tau(c, s);
+      warp_drop_below(s);
+    }
+  }
   if (mode == MODE_GREEDY) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
@@ -2051,7 +2289,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
 // host side
 // ---------------------------------------------------------------------------
 struct Layout {
-  uint32_t off_bar, off_cand, off_bits, off_pre, off_cnt, off_colr, off_tacc, off_misc, total;
+  uint32_t off_bar, off_cand, off_bits, off_pre, off_cnt, off_colr, off_pval, off_tacc, off_misc, total;
 };
 
 static uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
@@ -2075,6 +2313,8 @@ static Layout make_layout(int nwords, int cnt_cap, int n_tiles_all) {
   L.off_cnt = o;
   o += uint32_t(cnt_cap) * 4;
   L.off_colr = o;
+  o += uint32_t(cnt_cap) * 4;
+  L.off_pval = o;
   o += uint32_t(cnt_cap) * 4;
   o = align_up(o, 16);
   L.off_tacc = o;  // GENERAL: per-(warp, tile) mass (fixed point) and tie count
@@ -2136,6 +2376,7 @@ static int launch(const KArgs& base, int64_t batch, ns_stream_t stream) {
   a.off_pre = L.off_pre;
   a.off_cnt = L.off_cnt;
   a.off_colr = L.off_colr;
+  a.off_pval = L.off_pval;
   a.off_tacc = L.off_tacc;
   a.off_misc = L.off_misc;
   if (int(L.total) > di->max_smem_optin) return NS_ERR_INVALID_ARGUMENT;
