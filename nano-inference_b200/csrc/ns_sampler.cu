@@ -68,6 +68,9 @@ constexpr int kCandBytes = kWarps * kCapW * 8;  // candidate buffers (x, col)
 constexpr int kBins = 256;                      // radix digit = 8 bits (one bin per thread)
 static_assert(kBins == kThreads, "block_kth_regs clears one bin per thread");
 constexpr int kMaxCluster = 8;
+// leader merge area in the stage bytes: y[] and id[] lists, then u64 sort keys
+constexpr int kMergeCap = 4096;
+static_assert(kMergeCap * 16 <= kStageBytes, "merge lists and their sort keys fit the stage area");
 constexpr int kMaxLists = kMaxCluster * kWarps;
 constexpr unsigned kFull = 0xFFFFFFFFu;
 
@@ -190,6 +193,7 @@ struct Ctx {
   bool pen;  // this row has a history and a non-neutral penalty
   float Tabs;
   float rep, pres, freq;
+  float u_pre;  // the row's caller-supplied uniform (loaded when the kernel starts)
 
   __device__ __forceinline__ int w0(int w) const { return min(c0 + w * pw, c1); }
   __device__ __forceinline__ int w1(int w) const { return min(c0 + (w + 1) * pw, c1); }
@@ -1060,20 +1064,19 @@ __device__ __forceinline__ int status_from_flags(int f, bool greedy) {
 
 constexpr int kSmallN = 128;
 
+template <int DT>
+__device__ void finalize_small_sorted(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, int n);
+
 // Leader, FAST rows with n <= kSmallN survivors: sort by rank counting (thread
 // i owns survivor i), then one warp computes the softmax prefix sums with
 // shuffles (4 positions per lane).
 template <int DT>
 __device__ void finalize_small(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, int n) {
-  Misc* m = c.m;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x;
   const float* my = reinterpret_cast<const float*>(c.stages);
   const int* mid = reinterpret_cast<const int*>(c.stages + size_t(a.merge_cap) * 4);
   float* sy = reinterpret_cast<float*>(c.stages + size_t(a.merge_cap) * 8);
   int* sid = reinterpret_cast<int*>(sy + kSmallN);
-  float* se = reinterpret_cast<float*>(sid + kSmallN);
-  int* kid = reinterpret_cast<int*>(se + kSmallN);
-  float* kw = reinterpret_cast<float*>(kid + kSmallN);
   if (tid < n) {  // position in (y desc, id asc) order
     const float yi = my[tid] + 0.0f;
     const int ii = mid[tid];
@@ -1086,6 +1089,21 @@ __device__ void finalize_small(const Ctx<DT>& c, const KArgs& a, int64_t row, fl
     sid[rank] = ii;
   }
   __syncthreads();
+  finalize_small_sorted(c, a, row, topp, n);
+}
+
+// Leader, FAST rows: n <= kSmallN survivors already in (y desc, id asc) order
+// in sy[] / sid[]; one warp computes the softmax prefix sums with shuffles (4
+// positions per lane).
+template <int DT>
+__device__ void finalize_small_sorted(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, int n) {
+  Misc* m = c.m;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* sy = reinterpret_cast<float*>(c.stages + size_t(a.merge_cap) * 8);
+  int* sid = reinterpret_cast<int*>(sy + kSmallN);
+  float* se = reinterpret_cast<float*>(sid + kSmallN);
+  int* kid = reinterpret_cast<int*>(se + kSmallN);
+  float* kw = reinterpret_cast<float*>(kid + kSmallN);
   const float M = sy[0];
   if (!(M < INFINITY)) {
     if (tid == 0) a.out_ids[row] = NS_ERR_INVALID_DISTRIBUTION;
@@ -1136,7 +1154,7 @@ __device__ void finalize_small(const Ctx<DT>& c, const KArgs& a, int64_t row, fl
   __syncthreads();
   if (warp == 0) {
     // inverse CDF: the first kept id whose running weight exceeds u * total
-    const float u = a.uniforms ? a.uniforms[row] : philox_uniform(a.seed, a.offset, uint64_t(row));
+    const float u = a.uniforms ? c.u_pre : philox_uniform(a.seed, a.offset, uint64_t(row));
     double e[4], local = 0.0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -1218,7 +1236,7 @@ __device__ void finalize_row(const Ctx<DT>& c, const KArgs& a, int64_t row, floa
     keys[i] = (i < L) ? ((uint64_t(uint32_t(mid[i])) << 32) | uint64_t(__float_as_uint(my[i]))) : ~0ull;
   __syncthreads();
   bitonic_sort_u64(keys, n3, false);
-  const float u = a.uniforms ? a.uniforms[row] : philox_uniform(a.seed, a.offset, uint64_t(row));
+  const float u = a.uniforms ? c.u_pre : philox_uniform(a.seed, a.offset, uint64_t(row));
   if (tid == 0) m->choose = INT_MAX;
   __syncthreads();
   int first = INT_MAX;
@@ -1294,6 +1312,98 @@ __device__ __forceinline__ bool block_kth_regs(Misc* m, const uint32_t (&key)[R]
   }
   *out_key = prefix;
   return true;
+}
+
+// Leader, FAST rows whose union of survivors has at most kRankMax entries:
+// every survivor becomes the key (f2key(y) << 32) | ~id, y = rn(x / |T|), so
+// keys order by (y desc, id asc) and are distinct.  gather_keys copies the
+// union (read through distributed shared memory) before the cluster's last
+// barrier; rank_finalize sorts it by counting, for each key, the keys above
+// it, and takes the top-k with its ties at the k-th scaled value.
+constexpr int kRankMax = 1024;
+// keys[kRankMax] and sorted[kRankMax] in the stage area, past the merge lists
+// (y, id: kMergeCap * 8 bytes), finalize_small's arrays (5 * kSmallN * 4) and
+// finalize_row's sort keys for up to kRankMax survivors
+constexpr size_t kRankKeysOff = size_t(kMergeCap) * 8 + size_t(kRankMax) * 8;
+static_assert(size_t(kMergeCap) * 8 + 5 * kSmallN * 4 <= size_t(kMergeCap) * 8 + size_t(kRankMax) * 8,
+              "finalize_small's arrays fit below the rank keys");
+static_assert(kRankKeysOff + 2 * size_t(kRankMax) * 8 <= size_t(kStageBytes), "rank-sort keys fit the stage area");
+
+template <int DT>
+__device__ __forceinline__ void gather_keys(const Ctx<DT>& c, cg::cluster_group& cluster, int CL) {
+  Misc* m = c.m;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint64_t* keys = reinterpret_cast<uint64_t*>(c.stages + kRankKeysOff);
+  const int nl = CL * kWarps;
+  for (int l = warp; l < nl; l += kWarps) {
+    const int r = l / kWarps, wl = l % kWarps;
+    const int o = m->roff[l], nlst = m->roff[l + 1] - o;
+    const float* rcx = cluster.map_shared_rank(c.cx, r) + wl * kCapW;
+    const int* rcid = cluster.map_shared_rank(c.cid, r) + wl * kCapW;
+    const int c0r = m->rc0[r];
+    for (int i = lane; i < nlst; i += 32) {
+      const float y = __fdiv_rn(rcx[i], c.Tabs) + 0.0f;  // -0 and +0 tie
+      keys[o + i] = (uint64_t(f2key(y)) << 32) | uint64_t(~uint32_t(rcid[i] + c0r));
+    }
+  }
+  if (threadIdx.x == 0 && (m->roff[nl] & 1)) keys[m->roff[nl]] = 0ull;  // pad to whole pairs
+}
+
+template <int DT>
+__device__ void rank_finalize(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, int n) {
+  Misc* m = c.m;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const uint64_t* keys = reinterpret_cast<const uint64_t*>(c.stages + kRankKeysOff);
+  uint64_t* sorted = reinterpret_cast<uint64_t*>(c.stages + kRankKeysOff) + kRankMax;
+  if (n == 0) {
+    if (tid == 0) a.out_ids[row] = NS_ERR_INVALID_DISTRIBUTION;
+    return;
+  }
+  for (int i = tid; i < n; i += kThreads) {
+    const uint64_t ki = keys[i];
+    int r0 = 0, r1 = 0;
+#pragma unroll 4
+    for (int j = 0; j < n; j += 2) {
+      const ulonglong2 p = *reinterpret_cast<const ulonglong2*>(keys + j);
+      r0 += (p.x > ki) ? 1 : 0;
+      r1 += (p.y > ki) ? 1 : 0;
+    }
+    sorted[r0 + r1] = ki;
+  }
+  __syncthreads();
+  // top-k keeps every key whose scaled value ties the k-th (reference
+  // sampler.py:116-121); each warp finds the end of the tie run itself
+  const int kk = min(c.K, n);
+  const uint32_t yk = uint32_t(sorted[kk - 1] >> 32);
+  int nfin = n;
+  for (int j0 = kk; j0 < n; j0 += 32) {
+    const int j = j0 + lane;
+    const unsigned b = __ballot_sync(kFull, j < n && uint32_t(sorted[j] >> 32) < yk);
+    if (b) {
+      nfin = j0 + __ffs(b) - 1;
+      break;
+    }
+  }
+  if (nfin <= kSmallN) {
+    float* sy = reinterpret_cast<float*>(c.stages + size_t(a.merge_cap) * 8);
+    int* sid = reinterpret_cast<int*>(sy + kSmallN);
+    if (tid < nfin) {
+      sy[tid] = key2f(uint32_t(sorted[tid] >> 32));
+      sid[tid] = int(~uint32_t(sorted[tid]));
+    }
+    __syncthreads();
+    finalize_small_sorted(c, a, row, topp, nfin);
+    return;
+  }
+  float* my = reinterpret_cast<float*>(c.stages);
+  int* mid = reinterpret_cast<int*>(c.stages + size_t(a.merge_cap) * 4);
+  for (int i = tid; i < nfin; i += kThreads) {
+    my[i] = key2f(uint32_t(sorted[i] >> 32));
+    mid[i] = int(~uint32_t(sorted[i]));
+  }
+  if (tid == 0) m->n_merge = nfin;
+  __syncthreads();
+  finalize_row(c, a, row, topp);
 }
 
 // Leader, FAST rows: the K-th largest value over the union of every warp list
@@ -1779,7 +1889,7 @@ __device__ void general_row(const Ctx<DT>& c, const KArgs& a, cg::cluster_group&
   const bool timed_out = (cluster_flags() & F_TIMEOUT) != 0;
   unsigned long long ZS = 0;
   for (int r = 0; r < CL; ++r) ZS += cl.map_shared_rank(m, r)->g_mass;
-  const float u = a.uniforms ? a.uniforms[c.row] : philox_uniform(a.seed, a.offset, uint64_t(c.row));
+  const float u = a.uniforms ? c.u_pre : philox_uniform(a.seed, a.offset, uint64_t(c.row));
   const unsigned long long target = (unsigned long long)(double(u) * double(ZS));
   int rsel = -1, rlast = -1;
   unsigned long long rbefore = 0, run = 0;
@@ -1985,6 +2095,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
   c.rep = rep;
   c.pres = pres;
   c.freq = freq;
+  c.u_pre = a.uniforms ? a.uniforms[row] : 0.0f;
   // The first kHB * kThreads history ids are loaded before any tile copy is
   // queued, and stay in registers for both prologue passes.
   constexpr int kHB = 8;
@@ -2279,10 +2390,20 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
       }
     }
     __syncthreads();
-    if (mode == MODE_FAST && status_from_flags(m->flags, false) == NS_OK) leader_gather(c, a, cluster, CL);
+    if (mode == MODE_FAST && status_from_flags(m->flags, false) == NS_OK) {
+      if (m->roff[CL * kWarps] <= kRankMax)
+        gather_keys(c, cluster, CL);
+      else
+        leader_gather(c, a, cluster, CL);
+    }
   }
   cluster.sync();
-  if (rank == 0 && mode == MODE_FAST && status_from_flags(m->flags, false) == NS_OK) finalize_row(c, a, row, topp);
+  if (rank == 0 && mode == MODE_FAST && status_from_flags(m->flags, false) == NS_OK) {
+    if (m->roff[CL * kWarps] <= kRankMax)
+      rank_finalize(c, a, row, topp, m->roff[CL * kWarps]);
+    else
+      finalize_row(c, a, row, topp);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -2368,8 +2489,7 @@ static int launch(const KArgs& base, int64_t batch, ns_stream_t stream) {
   a.nwords = a.hist_ids ? int((span + 31) / 32) : 0;
   a.cnt_cap = a.hist_ids ? int(std::min<int64_t>(std::max<int64_t>(a.max_history, 1), span)) : 0;
   const Layout L = make_layout(a.nwords, a.cnt_cap, n_tiles_all);
-  a.merge_cap = 1;
-  while (a.merge_cap * 2 * 16 <= kStageBytes) a.merge_cap <<= 1;
+  a.merge_cap = kMergeCap;
   a.off_bar = L.off_bar;
   a.off_cand = L.off_cand;
   a.off_bits = L.off_bits;

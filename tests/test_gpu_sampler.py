@@ -169,6 +169,23 @@ def test_negative_temperature_and_ties(sampler):
     check(ids, ref, "ties")
 
 
+@pytest.mark.parametrize("n_ties,K,B", [(300, 100, 2), (1500, 100, 2), (1500, 100, 200)])
+def test_tie_plateau_merge_paths(sampler, n_ties, K, B):
+    """A plateau of equal maxima larger than K: every tie is kept (reference
+    top-k keeps values equal to the k-th).  300 ties reach the rank-sort merge
+    with more than 128 kept survivors; 1500 exceed the rank-sort capacity, in
+    cluster (B=2) and single-block (B=200) launches."""
+    V = 151936
+    rng = np.random.default_rng(n_ties * 7 + B)
+    x = make_logits(n_ties + B, B, V, 1.0)
+    for b in range(B):
+        x[b, rng.choice(V, n_ties, replace=False)] = 9.0
+    params = [SamplingParams(temperature=1.0, top_k=K, top_p=0.95)] * B
+    u = make_uniforms(n_ties + 1, B)
+    ids, ref = run(sampler, x, [[]] * B, params, u)
+    check(ids, ref, f"ties {n_ties} B={B}")
+
+
 def test_philox_default_stream_matches_oracle(sampler):
     from b200_sampler import B200Sampler
     s = B200Sampler(seed=99)
