@@ -429,6 +429,13 @@ __device__ __forceinline__ void warp_append_bits(const Ctx<DT>& c, WarpCand& s, 
 // tail); issued by lane 0 of the owning warp
 // ---------------------------------------------------------------------------
 template <int DT>
+__device__ __forceinline__ void issue_full_tile(const Ctx<DT>& c, int w, int t, int s, uint64_t policy) {
+  const uint8_t* src = c.rowp + size_t(c.w0(w) + t * Ctx<DT>::TE) * Ctx<DT>::ES;
+  mbar_arrive_expect_tx(c.sbar(w, s), kWTile);
+  bulk_g2s(c.stage(w, s), src, kWTile, c.sbar(w, s), policy);
+}
+
+template <int DT>
 __device__ void issue_tile(const Ctx<DT>& c, int w, int t, int s, uint64_t policy) {
   using E = Elem<DT>;
   constexpr int ES = E::size;
@@ -493,10 +500,37 @@ __device__ __forceinline__ void patch_tile(const Ctx<DT>& c, int w, int t, uint8
   fence_proxy_async_smem();  // the slots are rewritten by a later bulk copy
 }
 
-// Penalise without emitting (the values are taken from pval[] later).
+// Streaming passes: the history slots become -inf and their raw values go to
+// pval[]; penalize_segment() turns them into penalised values once the warp's
+// tiles are done.
 template <int DT>
 __device__ __forceinline__ void mask_tile(const Ctx<DT>& c, int w, int t, uint8_t* st) {
-  patch_tile(c, w, t, st, [](bool, float, int) {});
+  using E = Elem<DT>;
+  using R = typename E::raw;
+  if (!c.pen) return;
+  const int lane = threadIdx.x & 31;
+  const int2 rr = tile_ranks(c, w, t);
+  if (rr.y <= rr.x) return;
+  const int base = w * c.pw + t * Ctx<DT>::TE;
+  const int lead = c.tile_lead(w, t);
+  R* sr = reinterpret_cast<R*>(st);
+  for (int ri = rr.x + lane; ri < rr.y; ri += 32) {
+    const int e = lead + (c.colr[ri] - base);
+    c.pval[ri] = E::widen(sr[e]);
+    sr[e] = c.neg ? E::pinf : E::ninf;
+  }
+  fence_proxy_async_smem();  // the slots are rewritten by a later bulk copy
+}
+
+// Penalise the raw values mask_tile() recorded for warp w's columns.
+template <int DT>
+__device__ __forceinline__ void penalize_segment(const Ctx<DT>& c, int w) {
+  const int lane = threadIdx.x & 31;
+  for (int r = c.m->segoff[w] + lane; r < c.m->segoff[w + 1]; r += 32) {
+    const float x = penalize(c.pval[r], c.cnt[r], c.rep, c.pres, c.freq);
+    c.pval[r] = c.neg ? -x : x;
+  }
+  __syncwarp();
 }
 
 // ---------------------------------------------------------------------------
@@ -685,13 +719,13 @@ __device__ __forceinline__ void greedy_full(const uint8_t* st, int colbase, floa
 // with its own vote; the common group is a shared load, a compare chain and
 // a vote.
 template <int DT, bool NEG>
-__device__ __forceinline__ void fast_tile(const Ctx<DT>& c, WarpCand& s, int w, int t, const uint8_t* st) {
+__device__ __forceinline__ void fast_tile(const Ctx<DT>& c, WarpCand& s, int w, int t, const uint8_t* st, bool full) {
   constexpr int VE = Ctx<DT>::VE, TE = Ctx<DT>::TE;
   const int lane = threadIdx.x & 31;
   const int len = c.tile_len(w, t), lead = c.tile_lead(w, t);
   const int n_groups = (lead + len + VE - 1) / VE;
   const int colbase = w * c.pw + t * TE - lead;  // CTA-relative column of slot 0
-  if (len == TE && lead == 0) {
+  if (full) {
     fast_full<DT, NEG>(c, s, st, colbase);
     return;
   }
@@ -744,13 +778,13 @@ __device__ __forceinline__ void greedy_group(const float (&x)[Ctx<DT>::VE], int 
 
 template <int DT>
 __device__ __forceinline__ void greedy_tile(const Ctx<DT>& c, int w, int t, const uint8_t* st, float& best,
-                                            int& bidx) {
+                                            int& bidx, bool full) {
   constexpr int VE = Ctx<DT>::VE, TE = Ctx<DT>::TE;
   const int lane = threadIdx.x & 31;
   const int len = c.tile_len(w, t), lead = c.tile_lead(w, t);
   const int n_groups = (lead + len + VE - 1) / VE;
   const int colbase = c.c0 + w * c.pw + t * TE - lead;  // call-local column of slot 0
-  if (len == TE && lead == 0) {
+  if (full) {
     greedy_full<DT>(st, colbase, best, bidx);
     return;
   }
@@ -764,14 +798,23 @@ __device__ __forceinline__ void greedy_tile(const Ctx<DT>& c, int w, int t, cons
   }
 }
 
+// Leading tiles of warp w that are full and start on a 16-byte boundary (the
+// register paths and single-copy issue); the alignment is the same for every
+// tile of the warp because a tile is a multiple of 16 bytes.
+template <int DT>
+__device__ __forceinline__ int full_tiles(const Ctx<DT>& c, int w) {
+  if (c.w1(w) <= c.w0(w) || c.tile_head(w, 0) != 0) return 0;
+  return (c.w1(w) - c.w0(w)) / Ctx<DT>::TE;
+}
+
 // Largest finite value of the lane's slots of a landed tile in the filter
 // domain (-inf if none; a lane holding a NaN or +inf contributes nothing).
 template <int DT, bool NEG>
 __device__ __forceinline__ float tile_lane_max(const Ctx<DT>& c, int w, int t, const uint8_t* st) {
-  constexpr int VE = Ctx<DT>::VE, TE = Ctx<DT>::TE;
+  constexpr int VE = Ctx<DT>::VE;
   const int lane = threadIdx.x & 31;
   const int len = c.tile_len(w, t), lead = c.tile_lead(w, t);
-  if (len == TE && lead == 0) {
+  if (t < full_tiles(c, w)) {
     uint4 v[kGroupsPerLane<DT>];
     load_full<DT>(st, v);
     float m = -INFINITY;
@@ -824,36 +867,6 @@ __device__ __forceinline__ uint32_t warp_kth_lanes(uint32_t key, int kq) {
   return res;
 }
 
-// kq-th largest (with multiplicity) of the warp's buffer; 0 if fewer entries.
-__device__ __forceinline__ uint32_t warp_kth_buffer(const WarpCand& s, int kq) {
-  const int lane = threadIdx.x & 31;
-  if (s.n < kq) return 0u;
-  uint32_t key[kPerLane];
-#pragma unroll
-  for (int q = 0; q < kPerLane; ++q) {
-    const int i = q * 32 + lane;
-    key[q] = (i < s.n) ? f2key(s.x[i]) : 0u;
-  }
-  uint32_t res = 0;
-  for (int j = 0; j < kq; ++j) {
-    uint32_t lm = key[0];
-#pragma unroll
-    for (int q = 1; q < kPerLane; ++q) lm = max(lm, key[q]);
-    res = __reduce_max_sync(kFull, lm);
-    const unsigned b = __ballot_sync(kFull, lm == res);
-    if (lane == __ffs(b) - 1) {
-      bool done = false;
-#pragma unroll
-      for (int q = 0; q < kPerLane; ++q)
-        if (!done && key[q] == res) {
-          key[q] = 0u;
-          done = true;
-        }
-    }
-  }
-  return res;
-}
-
 // Raise tau to the shared bound (all lanes call).
 template <int DT>
 __device__ __forceinline__ void read_shared_tau(const Ctx<DT>& c, WarpCand& s) {
@@ -875,10 +888,19 @@ __device__ __forceinline__ void publish_key(const Ctx<DT>& c, uint32_t v) {
   __syncwarp();
 }
 
+// The kq-th largest of the per-lane maxima of the buffer: kq distinct held
+// elements are at or above it.
 template <int DT>
 __device__ __forceinline__ void publish_bound(const Ctx<DT>& c, const WarpCand& s) {
   if (s.ovf) return;
-  publish_key(c, warp_kth_buffer(s, share_kq(c.K)));
+  const int lane = threadIdx.x & 31;
+  uint32_t lm = 0;
+#pragma unroll
+  for (int q = 0; q < kPerLane; ++q) {
+    const int i = q * 32 + lane;
+    if (i < s.n) lm = max(lm, f2key(s.x[i]));
+  }
+  publish_key(c, warp_kth_lanes(lm, share_kq(c.K)));
 }
 
 // Stream this warp's tiles from t_begin (its first kWStages copies were issued
@@ -890,6 +912,7 @@ __device__ __forceinline__ bool stream_warp(const Ctx<DT>& c, int mode, uint64_t
                                             WarpCand& s, float& best, int& bidx) {
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nt = c.wtiles(w);
+  const int nfull = full_tiles(c, w);
   for (int t = t_begin; t < nt; ++t) {
     const int sidx = t % kWStages;
     uint8_t* st = c.stage(w, sidx);
@@ -910,17 +933,23 @@ __device__ __forceinline__ bool stream_warp(const Ctx<DT>& c, int mode, uint64_t
       }
     }
     if (mode == MODE_GREEDY) {
-      greedy_tile(c, w, t, st, best, bidx);
+      greedy_tile(c, w, t, st, best, bidx, t < nfull);
     } else if (!s.ovf) {
       if (c.neg)
-        fast_tile<DT, true>(c, s, w, t, st);
+        fast_tile<DT, true>(c, s, w, t, st, t < nfull);
       else
-        fast_tile<DT, false>(c, s, w, t, st);
-      if ((t & 3) == 1) publish_bound(c, s);
+        fast_tile<DT, false>(c, s, w, t, st, t < nfull);
+      if (t == 1 || t == 4 || t == 9) publish_bound(c, s);
       read_shared_tau(c, s);
     }
     __syncwarp();
-    if (lane == 0 && t + kWStages < nt) issue_tile(c, w, t + kWStages, (t + kWStages) % kWStages, policy);
+    if (lane == 0 && t + kWStages < nt) {
+      const int tn = t + kWStages;
+      if (tn < nfull)
+        issue_full_tile(c, w, tn, tn % kWStages, policy);
+      else
+        issue_tile(c, w, tn, tn % kWStages, policy);
+    }
   }
   return true;
 }
@@ -2283,9 +2312,9 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
   }
   bool ok = true;
   if (streams) ok = stream_warp(c, mode, policy, 0, n_ready, s, best, bidx);
-  // this warp's penalised history values (computed as its tiles landed): the
-  // rank range of its columns
+  // this warp's penalised history values: the rank range of its columns
   if (ok && c.pen) {
+    penalize_segment(c, warp);
     const int hr0 = m->segoff[warp], hr1 = m->segoff[warp + 1];
     if (mode == MODE_GREEDY) {
       for (int r = hr0 + lane; r < hr1; r += 32) {
