@@ -9,8 +9,9 @@ reference publishes no benchmark data).
 
 One step = one ``ns_sample`` launch over one batch.  ``value`` is sampled
 tokens/s over all ranks with inputs resident in HBM, timed with CUDA events
-around a CUDA-graph replay of K launches that rotate over 3 logits buffers
-(467 MB in total, > the 126 MB L2), max over ranks.  ``e2e`` is the same
+around CUDA-graph replays totalling exactly K launches (graphs of up to
+GRAPH_LAUNCHES launches) that rotate over 3 logits buffers (467 MB in total,
+> the 126 MB L2), max over ranks.  ``e2e`` is the same
 metric through the public ``B200Sampler.select_batch`` call with the logits
 in pinned host memory and the histories as Python lists (H2D copies, packing
 and the ids' D2H read inside the timed region).
@@ -39,6 +40,11 @@ import torch  # noqa: E402
 METRIC = "sampled tokens/sec and logits HBM GB/s vs peak at B=256,V=151936"
 UNIT = "tokens/s"
 N_BUFFERS = 3
+GRAPH_LAUNCHES = 500
+# DRAM bytes (read + write) of one headline launch of the sampling kernel,
+# from the ncu capture summarised in profiles/sample_kernel_headline_B256.md
+# (dram__bytes_read.sum + dram__bytes_write.sum of one launch, same workload).
+NCU_TRAFFIC_BYTES = 156769792 + 3456512
 
 
 def _peaks():
@@ -170,26 +176,32 @@ def cpu_port_tokens_per_s(w, rows: int, steps: int = 1, threads: int = 1):
 
 
 def run_reference(args, world, rank):
+    """The CPU reference arm: rows of the headline workload through the numpy
+    restatement, all host threads across rows.  A step is one round of
+    `threads` rows; the run stops after the requested steps or a ~90 s budget,
+    whichever comes first, and reports both counts."""
     if rank != 0:
         return
     from b200_sampler.workloads import headline
     w = headline()
     threads = os.cpu_count() or 1
-    # size the per-step sample so the whole run stays within about two minutes
-    probe_rate, _ = cpu_port_tokens_per_s(w, 2, 1, 1)
-    total_steps = args.steps + args.warmup
-    rows = int(max(1, min(w.batch, probe_rate * max(threads // 2, 1) * 100.0 / max(total_steps, 1))))
-    for _ in range(args.warmup):
+    rows = min(w.batch, threads)
+    cpu_port_tokens_per_s(w, rows, 1, threads)                      # warm-up round
+    _, t_round = cpu_port_tokens_per_s(w, rows, 1, threads)
+    steps_run = int(max(1, min(args.steps, 90.0 / max(t_round, 1e-6))))
+    for _ in range(min(args.warmup, 1)):
         cpu_port_tokens_per_s(w, rows, 1, threads)
-    rate, dt = cpu_port_tokens_per_s(w, rows, args.steps, threads)
-    cfg = {"workload": w.notes, "sample_rows_per_step": rows, "rows_per_step_full": w.batch}
+    rate, dt = cpu_port_tokens_per_s(w, rows, steps_run, threads)
+    cfg = {"workload": w.notes, "sample_rows_per_step": rows, "rows_per_step_full": w.batch,
+           "steps_requested": args.steps, "steps_run": steps_run}
     line = {"impl": "reference", "metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3 * w.batch / rows,
+            "steps": steps_run, "warmup": args.warmup, "ms_per_step": w.batch / rate * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded randn*3 logits, uniform histories)", "config": cfg,
             "cpu_baseline": {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
                              "sample": f"{rows} of {w.batch} rows of the headline workload per step, "
-                                       f"numpy restatement of Sampler.select_batch, {threads} threads"},
+                                       f"{steps_run} steps, numpy restatement of Sampler.select_batch, "
+                                       f"{threads} threads"},
             "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -247,13 +259,22 @@ def run_ours(args, world, rank, local):
             assert db.launch(bufs[i % N_BUFFERS], out, stream) == 0
     stream.synchronize()
 
-    # one CUDA graph with K launches rotating over the buffers
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=stream):
-        for i in range(args.steps):
-            db.launch(bufs[i % N_BUFFERS], out, torch.cuda.current_stream(dev))
+    # CUDA graphs of up to GRAPH_LAUNCHES launches rotating over the buffers;
+    # `reps` replays of the full graph plus one of the remainder make K steps
+    def capture(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(n):
+                db.launch(bufs[i % N_BUFFERS], out, torch.cuda.current_stream(dev))
+        return g
+    per = min(args.steps, GRAPH_LAUNCHES)
+    reps, rem = divmod(args.steps, per)
+    g = capture(per)
+    g_rem = capture(rem) if rem else None
     with torch.cuda.stream(stream):
         g.replay()                                   # graph warm-up
+        if g_rem is not None:
+            g_rem.replay()
     stream.synchronize()
 
     e0 = torch.cuda.Event(enable_timing=True)
@@ -263,7 +284,10 @@ def run_ours(args, world, rank, local):
     with ClockSampler(local) as clk:
         with torch.cuda.stream(stream):
             e0.record(stream)
-            g.replay()
+            for _ in range(reps):
+                g.replay()
+            if g_rem is not None:
+                g_rem.replay()
             e1.record(stream)
         stream.synchronize()
     barrier(world)
@@ -276,7 +300,7 @@ def run_ours(args, world, rank, local):
     peak, peak_kind = _peaks()
     alg = algorithmic_bytes(B, V, H)
     achieved = alg / (ms / args.steps / 1e3) / 1e9
-    del g
+    del g, g_rem
 
     # ---- end to end through the public API, host buffers ----
     e2e = None
@@ -289,10 +313,13 @@ def run_ours(args, world, rank, local):
             "config": {"workload": w.notes, "global_batch": B * world, "rows_per_gpu": B, "vocab": V,
                        "parallelism": f"rows sharded, {world} GPU(s), no collective",
                        "l2": f"{N_BUFFERS} rotating logits buffers ({N_BUFFERS * B * V * 4 / 1e6:.0f} MB) > L2",
-                       "timing": "CUDA graph of K launches, CUDA events, max over ranks"},
+                       "timing": f"CUDA graphs ({per} launches x {reps} replays"
+                                 f"{f' + {rem}' if rem else ''}), CUDA events, max over ranks"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
-                         "algorithmic_bytes_per_launch": alg},
+                         "frac": achieved / peak, "traffic": NCU_TRAFFIC_BYTES, "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": alg,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
+                                           "(profiles/sample_kernel_headline_B256.md)"},
             "gpu_launches": args.steps}
     if e2e is not None:
         line["e2e"] = e2e
@@ -300,10 +327,14 @@ def run_ours(args, world, rank, local):
     if clocks is not None:
         line["clocks"] = clocks
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, dtc = cpu_port_tokens_per_s(w, 8, 1, 1)
+        # bounded sample: rows of the same workload until ~10 s of single-thread work
+        probe, _ = cpu_port_tokens_per_s(w, 2, 1, 1)
+        rows = int(max(2, min(w.batch, probe * 10.0)))
+        reps_c = int(max(1, min(100, 10.0 * probe / rows)))
+        rate, dtc = cpu_port_tokens_per_s(w, rows, reps_c, 1)
         line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": 1, "kind": "port",
-                                "sample": "8 of 256 rows of the headline workload, numpy restatement of "
-                                          "Sampler.select_batch, 1 thread"}
+                                "sample": f"{rows} of {w.batch} rows of the headline workload x {reps_c} "
+                                          f"({dtc:.1f} s), numpy restatement of Sampler.select_batch, 1 thread"}
     if rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -311,7 +342,7 @@ def run_ours(args, world, rank, local):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
