@@ -100,6 +100,46 @@ int ns_sample(const void* logits, int dtype, int64_t batch, int64_t vocab, int64
               const float* uniforms, uint64_t philox_seed, uint64_t philox_offset,
               int64_t* out_ids, void* workspace, size_t workspace_bytes, ns_stream_t stream);
 
+/*
+ * Vocab-parallel sampling (tensor-parallel lm_head output: each device holds
+ * a contiguous column slice of every row).  No reference counterpart: the
+ * reference samples whole rows only (sampler.py:36-91); these calls split that
+ * same computation into a local step, an all-gather of small per-row records
+ * (done by the caller, e.g. NCCL), and a merge that every rank runs on the
+ * same gathered bytes, so all ranks produce the same ids -- the ids ns_sample
+ * would produce on the whole rows.
+ *
+ * Record layout (int64): [batch] survivor counts (or negative ns_status),
+ * then [batch][cap] keys.  ns_vp_record_int64s gives its length.
+ */
+int ns_vp_record_int64s(int64_t batch, int cap, int64_t* out_count);
+
+/*
+ * Local step on this device's slice: columns [vocab_offset, vocab_offset +
+ * vocab_local) of a vocab_total-wide row.  History ids are global ids; each
+ * slice penalises the ones it holds.  Writes per row the top-k survivors
+ * (ties at the k-th value kept) as keys, or for greedy rows (T == 0) one key.
+ * Rows with top-k off or k > 128 report NS_ERR_UNSUPPORTED; more than `cap`
+ * survivors report NS_ERR_CANDIDATE_OVERFLOW.  cap in [1, 1024].
+ */
+int ns_vp_local(const void* logits, int dtype, int64_t batch, int64_t vocab_local, int64_t row_stride,
+                int64_t vocab_offset, int64_t vocab_total,
+                const int32_t* hist_ids, const int64_t* hist_offsets, int64_t max_history,
+                const float* temperature, const int32_t* top_k, const float* top_p,
+                const float* repetition_penalty, const float* presence_penalty,
+                const float* frequency_penalty, int cap, int64_t* record, ns_stream_t stream);
+
+/*
+ * Merge the all-gathered records (n_ranks consecutive records, rank order)
+ * into one id per row: global top-k with ties, top-p, inverse CDF with the
+ * row's uniform (or Philox as in ns_sample; the row index is the counter).
+ * out_ids as in ns_sample.  n_ranks in [1, 64].
+ */
+int ns_vp_merge(const int64_t* gathered, int n_ranks, int64_t batch, int cap, int64_t vocab_total,
+                const float* temperature, const int32_t* top_k, const float* top_p,
+                const float* uniforms, uint64_t philox_seed, uint64_t philox_offset,
+                int64_t* out_ids, ns_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -47,6 +47,21 @@ PROTOTYPES = {
         _c_vp, _c_u64, _c_u64,                       # uniforms, philox_seed, philox_offset
         _c_vp, _c_vp, _c_sz, _c_vp,                  # out_ids, workspace, workspace_bytes, stream
     ]),
+    "ns_vp_record_int64s": (_c_int, [_c_i64, _c_int, ctypes.POINTER(_c_i64)]),
+    "ns_vp_local": (_c_int, [
+        _c_vp, _c_int, _c_i64, _c_i64, _c_i64,       # logits, dtype, batch, vocab_local, row_stride
+        _c_i64, _c_i64,                              # vocab_offset, vocab_total
+        _c_vp, _c_vp, _c_i64,                        # hist_ids, hist_offsets, max_history
+        _c_vp, _c_vp, _c_vp,                         # temperature, top_k, top_p
+        _c_vp, _c_vp, _c_vp,                         # repetition, presence, frequency
+        _c_int, _c_vp, _c_vp,                        # cap, record, stream
+    ]),
+    "ns_vp_merge": (_c_int, [
+        _c_vp, _c_int, _c_i64, _c_int, _c_i64,       # gathered, n_ranks, batch, cap, vocab_total
+        _c_vp, _c_vp, _c_vp,                         # temperature, top_k, top_p
+        _c_vp, _c_u64, _c_u64,                       # uniforms, philox_seed, philox_offset
+        _c_vp, _c_vp,                                # out_ids, stream
+    ]),
 }
 
 _lock = threading.Lock()

@@ -87,6 +87,23 @@ class _Staging:
         return self.dev.data_ptr()
 
 
+class _Staged:
+    """Device pointers of one call's staged inputs."""
+
+    def __init__(self, params, p32, hist_ids, hist_offsets, max_hist, u_ptr, u_dev):
+        self.params = params          # host copy of the [6, B] block (numpy)
+        self.p32 = p32
+        self.hist_ids = hist_ids
+        self.hist_offsets = hist_offsets
+        self.max_hist = max_hist
+        self.u_ptr = u_ptr
+        self.u_dev = u_dev
+
+    def keep_alive(self, stream: torch.cuda.Stream):
+        if self.u_dev is not None:
+            self.u_dev.record_stream(stream)
+
+
 class B200Sampler(SamplerBase):
     """GPU sampler with the reference ``SamplerBase`` interface.
 
@@ -155,6 +172,27 @@ class B200Sampler(SamplerBase):
         if B == 0:
             return out
 
+        with self._lock:
+            st = self._stage(device, B, all_generated_ids, all_sampling_params, uniforms, stream)
+            offset = self.offset
+            self.offset += 1
+            rc = self.lib.ns_sample(
+                logits.data_ptr(), _DTYPES[logits.dtype], B, V, int(logits.stride(0)),
+                st.hist_ids, st.hist_offsets, st.max_hist,
+                st.p32, st.p32 + 4 * B, st.p32 + 8 * B,
+                st.p32 + 12 * B, st.p32 + 16 * B, st.p32 + 20 * B,
+                st.u_ptr, self.seed, offset,
+                out.data_ptr(), None, 0, stream.cuda_stream)
+            st.keep_alive(stream)
+        if rc != _lib.NS_OK:
+            raise RuntimeError(f"ns_sample failed: {_lib.status_string(rc)}")
+        return out
+
+    def _stage(self, device: torch.device, B: int, all_generated_ids, all_sampling_params,
+               uniforms: Optional[torch.Tensor], stream: torch.cuda.Stream) -> "_Staged":
+        """Pack params [6, B], the history CSR (only when a row has a
+        non-neutral penalty) and host uniforms into the pinned block, upload it
+        with one copy, and return the device pointers.  Call under the lock."""
         params = pack_params(all_sampling_params)                       # [6, B] 32-bit
         use_hist = all_generated_ids is not None and bool(
             (params[3] != 1.0).any() or (params[4] != 0.0).any() or (params[5] != 0.0).any())
@@ -172,52 +210,40 @@ class B200Sampler(SamplerBase):
         off_u = _align(off_ids + total * 4)
         nbytes = _align(off_u + (B * 4 if host_u else 0))
 
-        with self._lock:
-            stg = self._staging_for(device)
-            h = stg.reserve(nbytes)
-            h[off_params:off_params + 6 * B * 4] = params.reshape(-1).view(np.uint8)
-            if use_hist and total:
-                offs = h[off_offsets:off_offsets + (B + 1) * 8].view(np.int64)
-                offs[0] = 0
-                np.cumsum(lens, out=offs[1:])
-                flat = np.fromiter(itertools.chain.from_iterable(all_generated_ids), dtype=np.int64,
-                                   count=total)
-                if flat.min() < -(2 ** 31) or flat.max() >= 2 ** 31:
-                    raise IndexError(_lib.status_string(_lib.NS_ERR_TOKEN_ID_OUT_OF_RANGE))
-                h[off_ids:off_ids + total * 4].view(np.int32)[:] = flat
-            if host_u:
-                hu = uniforms.detach().to(torch.float32).reshape(-1).numpy()
-                if hu.size != B:
-                    raise ValueError("uniforms must have one value per row")
-                h[off_u:off_u + B * 4].view(np.float32)[:] = hu
-            base = stg.upload(nbytes, stream)
+        stg = self._staging_for(device)
+        h = stg.reserve(nbytes)
+        h[off_params:off_params + 6 * B * 4] = params.reshape(-1).view(np.uint8)
+        if use_hist and total:
+            offs = h[off_offsets:off_offsets + (B + 1) * 8].view(np.int64)
+            offs[0] = 0
+            np.cumsum(lens, out=offs[1:])
+            flat = np.fromiter(itertools.chain.from_iterable(all_generated_ids), dtype=np.int64,
+                               count=total)
+            if flat.min() < -(2 ** 31) or flat.max() >= 2 ** 31:
+                raise IndexError(_lib.status_string(_lib.NS_ERR_TOKEN_ID_OUT_OF_RANGE))
+            h[off_ids:off_ids + total * 4].view(np.int32)[:] = flat
+        if host_u:
+            hu = uniforms.detach().to(torch.float32).reshape(-1).numpy()
+            if hu.size != B:
+                raise ValueError("uniforms must have one value per row")
+            h[off_u:off_u + B * 4].view(np.float32)[:] = hu
+        base = stg.upload(nbytes, stream)
 
-            p32 = base + off_params
-            if uniforms is None:
-                u_ptr = 0
-            elif host_u:
-                u_ptr = base + off_u
-            else:
-                ud = uniforms.to(device=device, dtype=torch.float32).reshape(-1).contiguous()
-                if ud.numel() != B:
-                    raise ValueError("uniforms must have one value per row")
-                u_ptr = ud.data_ptr()
-            offset = self.offset
-            self.offset += 1
-            rc = self.lib.ns_sample(
-                logits.data_ptr(), _DTYPES[logits.dtype], B, V, int(logits.stride(0)),
-                (base + off_ids) if (use_hist and total) else None,
-                (base + off_offsets) if (use_hist and total) else None,
-                max_hist,
-                p32, p32 + 4 * B, p32 + 8 * B,
-                p32 + 12 * B, p32 + 16 * B, p32 + 20 * B,
-                u_ptr, self.seed, offset,
-                out.data_ptr(), None, 0, stream.cuda_stream)
-            if u_ptr and not host_u:
-                ud.record_stream(stream)
-        if rc != _lib.NS_OK:
-            raise RuntimeError(f"ns_sample failed: {_lib.status_string(rc)}")
-        return out
+        ud = None
+        if uniforms is None:
+            u_ptr = None
+        elif host_u:
+            u_ptr = base + off_u
+        else:
+            ud = uniforms.to(device=device, dtype=torch.float32).reshape(-1).contiguous()
+            if ud.numel() != B:
+                raise ValueError("uniforms must have one value per row")
+            u_ptr = ud.data_ptr()
+        has = use_hist and total > 0
+        return _Staged(params=params, p32=base + off_params,
+                       hist_ids=(base + off_ids) if has else None,
+                       hist_offsets=(base + off_offsets) if has else None,
+                       max_hist=max_hist, u_ptr=u_ptr, u_dev=ud)
 
     # -------------------------------------------------------------- helpers
     def _device_for(self, logits: torch.Tensor) -> torch.device:

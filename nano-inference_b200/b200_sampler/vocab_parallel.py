@@ -1,0 +1,178 @@
+"""Vocab-parallel sampling: each rank holds a contiguous column slice of every
+row (tensor-parallel lm_head output) and all ranks return the same ids.
+
+No reference counterpart: nano-inference samples whole rows
+(``sampling/sampler.py:36-91``).  The steps, per call:
+
+1. ``ns_vp_local`` on this rank's slice: history penalties for the ids the
+   slice holds, then per row the slice's top-k survivors (ties at the k-th
+   scaled value kept) as 64-bit keys, or one key for greedy rows;
+2. ``gather_records``: all-gather of those fixed-size records (NCCL over
+   NVLink; a few KB per row);
+3. ``ns_vp_merge`` on every rank: the global top-k with ties, top-p and the
+   inverse-CDF draw.  The global top-k set lies inside the union of the
+   slices' top-k sets, so the ids equal ``B200Sampler`` on whole rows.
+
+Rows with top-k off or k > 128 have no bounded candidate set; their slices are
+all-gathered into whole rows (``gather_full_rows``) and sampled with
+``ns_sample`` on every rank.  With ``uniforms=None`` those rows draw from the
+Philox stream at their position in that sub-batch (still identical on every
+rank).
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Sequence
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .params import pack_params
+from .sampler import _DTYPES, _ROW_ERRORS, B200Sampler
+
+FAST_MAX_K = 128       # largest top_k the candidate records serve (kFastK in the kernel)
+MAX_CAP = 1024         # record capacity limit (kRankMax in the kernel)
+
+
+def gather_records(rec: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather equal-length 1-D records; returns [world * len] in rank order."""
+    world = dist.get_world_size(group)
+    if world == 1:
+        return rec.contiguous()
+    out = torch.empty(world * rec.numel(), dtype=rec.dtype, device=rec.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, rec.contiguous(), group=group)
+    else:
+        dist.all_gather(list(out.view(world, -1).unbind(0)), rec.contiguous(), group=group)
+    return out
+
+
+def gather_full_rows(rows: torch.Tensor, offsets: Sequence[int], widths: Sequence[int], vocab_total: int,
+                     group=None) -> torch.Tensor:
+    """Rebuild whole rows from every rank's slice of the same rows: rows is
+    this rank's [n, width_r] slice; returns [n, vocab_total] on every rank."""
+    world = dist.get_world_size(group)
+    n = rows.shape[0]
+    wmax = max(widths)
+    pad = torch.zeros(n, wmax, dtype=rows.dtype, device=rows.device)
+    pad[:, :rows.shape[1]] = rows
+    g = gather_records(pad.reshape(-1), group).view(world, n, wmax)
+    full = torch.empty(n, vocab_total, dtype=rows.dtype, device=rows.device)
+    for r in range(world):
+        full[:, offsets[r]:offsets[r] + widths[r]] = g[r, :, :widths[r]]
+    return full
+
+
+class VocabParallelSampler(B200Sampler):
+    """``SamplerBase`` over a vocab-parallel slice.
+
+    Args:
+        vocab_total: full vocabulary size.
+        vocab_offset, vocab_local: this rank's columns
+            ``[vocab_offset, vocab_offset + vocab_local)``.
+        group: torch.distributed process group (default: the world).
+        seed: Philox key for calls without ``uniforms``; rank 0's value is
+            broadcast so every rank draws the same uniforms.
+        tie_slack: record entries beyond the batch's largest top_k for values
+            tied at a slice's k-th value; a row whose slice overflows is
+            retried once with the largest capacity.
+
+    Every rank must call with the same histories, params and uniforms (the
+    engine replicates them); the logits are this rank's slice.
+    """
+
+    def __init__(self, vocab_total: int, vocab_offset: int, vocab_local: int, group=None, device=None,
+                 seed: Optional[int] = None, tie_slack: int = 16):
+        super().__init__(device=device, seed=seed)
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.vocab_total = int(vocab_total)
+        self.vocab_offset = int(vocab_offset)
+        self.vocab_local = int(vocab_local)
+        self.tie_slack = int(tie_slack)
+        geo: List[Optional[tuple]] = [None] * self.world
+        dist.all_gather_object(geo, (self.vocab_offset, self.vocab_local, self.seed), group=group)
+        self.offsets = [g[0] for g in geo]
+        self.widths = [g[1] for g in geo]
+        self.seed = int(geo[0][2])
+        cover = sorted(zip(self.offsets, self.widths))
+        pos = 0
+        for o, w in cover:
+            if o != pos or w <= 0:
+                raise ValueError("rank slices must tile [0, vocab_total) without gaps or overlaps")
+            pos += w
+        if pos != self.vocab_total:
+            raise ValueError("rank slices must cover the whole vocabulary")
+
+    def select_batch_tensor(self, logits: torch.Tensor, all_generated_ids, all_sampling_params, *,
+                            uniforms: Optional[torch.Tensor] = None,
+                            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        return self._run(logits, all_generated_ids, all_sampling_params, uniforms, out, retry=True)
+
+    def _run(self, logits, all_generated_ids, all_sampling_params, uniforms, out, retry: bool,
+             cap: Optional[int] = None, offset: Optional[int] = None) -> torch.Tensor:
+        if logits.dim() != 2 or logits.shape[1] != self.vocab_local:
+            raise ValueError("expected this rank's [batch, vocab_local] slice")
+        if logits.dtype not in _DTYPES:
+            raise TypeError(f"unsupported logits dtype {logits.dtype}")
+        B = int(logits.shape[0])
+        if len(all_sampling_params) != B or (all_generated_ids is not None and len(all_generated_ids) != B):
+            raise AssertionError("batch size mismatch")
+        device = self._device_for(logits)
+        if logits.device != device:
+            logits = logits.to(device, non_blocking=True)
+        if logits.stride(1) != 1:
+            logits = logits.contiguous()
+        stream = torch.cuda.current_stream(device)
+        if out is None:
+            out = torch.empty(B, dtype=torch.int64, device=device)
+        if B == 0:
+            return out
+        params = pack_params(all_sampling_params)
+        temp = params[0]
+        top_k = params[1].view(np.int32)
+        sampled = temp != 0.0
+        fast = sampled & (top_k > 0) & (top_k <= FAST_MAX_K) & (top_k.astype(np.int64) < self.vocab_total)
+        general = np.nonzero(sampled & ~fast)[0].tolist()
+        if cap is None:
+            kmax = int(top_k[fast].max()) if fast.any() else 0
+            cap = min(MAX_CAP, max(1, kmax + self.tie_slack))
+        rec = torch.empty(B * (1 + cap), dtype=torch.int64, device=device)
+        with self._lock:
+            st = self._stage(device, B, all_generated_ids, all_sampling_params, uniforms, stream)
+            if offset is None:
+                offset = self.offset
+                self.offset += 1
+            rc = self.lib.ns_vp_local(
+                logits.data_ptr(), _DTYPES[logits.dtype], B, self.vocab_local, int(logits.stride(0)),
+                self.vocab_offset, self.vocab_total,
+                st.hist_ids, st.hist_offsets, st.max_hist,
+                st.p32, st.p32 + 4 * B, st.p32 + 8 * B, st.p32 + 12 * B, st.p32 + 16 * B, st.p32 + 20 * B,
+                cap, rec.data_ptr(), stream.cuda_stream)
+            if rc != _lib.NS_OK:
+                raise RuntimeError(f"ns_vp_local failed: {_lib.status_string(rc)}")
+            gathered = gather_records(rec, self.group)
+            rc = self.lib.ns_vp_merge(
+                gathered.data_ptr(), self.world, B, cap, self.vocab_total,
+                st.p32, st.p32 + 4 * B, st.p32 + 8 * B, st.u_ptr, self.seed, offset,
+                out.data_ptr(), stream.cuda_stream)
+            st.keep_alive(stream)
+            if rc != _lib.NS_OK:
+                raise RuntimeError(f"ns_vp_merge failed: {_lib.status_string(rc)}")
+        if general:
+            idx = torch.tensor(general, dtype=torch.long, device=device)
+            full = gather_full_rows(logits.index_select(0, idx), self.offsets, self.widths, self.vocab_total,
+                                    self.group)
+            hs = None if all_generated_ids is None else [all_generated_ids[b] for b in general]
+            ps = [all_sampling_params[b] for b in general]
+            us = None if uniforms is None else uniforms.reshape(-1)[idx.to(uniforms.device)]
+            sub = B200Sampler.select_batch_tensor(self, full, hs, ps, uniforms=us)
+            out.index_copy_(0, idx, sub)
+        if retry and cap < MAX_CAP:
+            # every rank merged the same bytes, so every rank takes the same branch
+            if bool((out == _lib.NS_ERR_CANDIDATE_OVERFLOW).any()):
+                return self._run(logits, all_generated_ids, all_sampling_params, uniforms, out, retry=False,
+                                 cap=MAX_CAP, offset=offset)
+        return out

@@ -161,6 +161,10 @@ struct KArgs {
   int nwords;      // history bitmap words (one bit per column of a CTA)
   int cnt_cap;     // distinct history ids the rank arrays hold
   int merge_cap;   // leader merge area (entries)
+  // vocab-parallel local step: out_ids[] receives each row's survivor count
+  // (or a negative status) and vp_keys[row * vp_cap ...] its sorted keys
+  int64_t* vp_keys;
+  int vp_cap;
   uint32_t off_bar, off_cand, off_bits, off_pre, off_cnt, off_colr, off_pval, off_tacc, off_misc;
 };
 
@@ -1379,13 +1383,15 @@ __device__ __forceinline__ void gather_keys(const Ctx<DT>& c, cg::cluster_group&
 }
 
 template <int DT>
+__device__ void finalize_keys(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, int n, int n_all);
+
+template <int DT>
 __device__ void rank_finalize(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, int n) {
-  Misc* m = c.m;
-  const int tid = threadIdx.x, lane = tid & 31;
+  const int tid = threadIdx.x;
   const uint64_t* keys = reinterpret_cast<const uint64_t*>(c.stages + kRankKeysOff);
   uint64_t* sorted = reinterpret_cast<uint64_t*>(c.stages + kRankKeysOff) + kRankMax;
-  if (n == 0) {
-    if (tid == 0) a.out_ids[row] = NS_ERR_INVALID_DISTRIBUTION;
+  if (n == 0) {  // nothing finite (a vocab-parallel slice may legitimately hold none)
+    if (tid == 0) a.out_ids[row] = a.vp_keys ? 0 : NS_ERR_INVALID_DISTRIBUTION;
     return;
   }
   for (int i = tid; i < n; i += kThreads) {
@@ -1400,8 +1406,22 @@ __device__ void rank_finalize(const Ctx<DT>& c, const KArgs& a, int64_t row, flo
     sorted[r0 + r1] = ki;
   }
   __syncthreads();
-  // top-k keeps every key whose scaled value ties the k-th (reference
-  // sampler.py:116-121); each warp finds the end of the tie run itself
+  finalize_keys(c, a, row, topp, n, n);
+}
+
+// The first n keys of the sorted union (descending) are in sorted[]; n_all >=
+// n survivors exist in total.  Top-k keeps every key whose scaled value ties
+// the k-th (reference sampler.py:116-121); each warp finds the end of the tie
+// run itself.  A tie run that reaches past the n placed keys overflows.
+template <int DT>
+__device__ void finalize_keys(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, int n, int n_all) {
+  Misc* m = c.m;
+  const int tid = threadIdx.x, lane = tid & 31;
+  uint64_t* sorted = reinterpret_cast<uint64_t*>(c.stages + kRankKeysOff) + kRankMax;
+  if (n == 0) {  // nothing finite (a vocab-parallel slice may legitimately hold none)
+    if (tid == 0) a.out_ids[row] = a.vp_keys ? 0 : NS_ERR_INVALID_DISTRIBUTION;
+    return;
+  }
   const int kk = min(c.K, n);
   const uint32_t yk = uint32_t(sorted[kk - 1] >> 32);
   int nfin = n;
@@ -1412,6 +1432,23 @@ __device__ void rank_finalize(const Ctx<DT>& c, const KArgs& a, int64_t row, flo
       nfin = j0 + __ffs(b) - 1;
       break;
     }
+  }
+  if (nfin == n && n_all > n) {
+    if (tid == 0) a.out_ids[row] = NS_ERR_CANDIDATE_OVERFLOW;
+    return;
+  }
+  if (a.vp_keys) {  // vocab-parallel local step: the survivors are the record
+    if (nfin > a.vp_cap) {
+      if (tid == 0) a.out_ids[row] = NS_ERR_CANDIDATE_OVERFLOW;
+      return;
+    }
+    int64_t* rk = a.vp_keys + row * a.vp_cap;
+    for (int i = tid; i < nfin; i += kThreads) {
+      const uint32_t gid = ~uint32_t(sorted[i]) + uint32_t(a.vocab_offset);
+      rk[i] = int64_t((sorted[i] & 0xFFFFFFFF00000000ull) | uint64_t(~gid));
+    }
+    if (tid == 0) a.out_ids[row] = nfin;
+    return;
   }
   if (nfin <= kSmallN) {
     float* sy = reinterpret_cast<float*>(c.stages + size_t(a.merge_cap) * 8);
@@ -2111,6 +2148,10 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     mode = MODE_FAST;
   else
     mode = MODE_GENERAL;
+  if (a.vp_keys && mode == MODE_GENERAL) {  // no candidate record for these rows
+    if (rank == 0 && tid == 0) a.out_ids[row] = NS_ERR_UNSUPPORTED;
+    return;
+  }
   c.neg = T < 0.0f;
   c.Tabs = fabsf(T);
   c.K = topk;
@@ -2381,6 +2422,11 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     int fl_all = 0;
     for (int r = 0; r < CL; ++r) fl_all |= cluster.map_shared_rank(m, r)->flags;
     const bool hard = (fl_all & (F_NAN | F_TIMEOUT | F_BADID | F_HIST)) != 0;
+    if (a.vp_keys && mode == MODE_FAST && (fl_all & F_OVF) && !hard) {
+      cluster.sync();  // every CTA has read the others' flags
+      if (rank == 0 && tid == 0) a.out_ids[row] = NS_ERR_CANDIDATE_OVERFLOW;
+      return;
+    }
     if (mode == MODE_GENERAL || (mode == MODE_FAST && (fl_all & F_OVF) && !hard)) {
       cluster.sync();
       if (tid == 0) m->flags &= ~F_OVF;
@@ -2413,26 +2459,166 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
       m->flags = fl;
       if (mode == MODE_GREEDY) {
         const int st = status_from_flags(fl, true);
-        a.out_ids[row] = (st != NS_OK) ? int64_t(st) : int64_t(bi) + a.vocab_offset;
+        if (st != NS_OK) {
+          a.out_ids[row] = int64_t(st);
+        } else if (a.vp_keys) {  // one key; NaN sorts above every value
+          const uint32_t hi = (b != b) ? 0xFFFFFFFFu : f2key(b + 0.0f);
+          const uint32_t gid = uint32_t(int64_t(bi) + a.vocab_offset);
+          a.vp_keys[row * a.vp_cap] = int64_t((uint64_t(hi) << 32) | uint64_t(~gid));
+          a.out_ids[row] = 1;
+        } else {
+          a.out_ids[row] = int64_t(bi) + a.vocab_offset;
+        }
       } else if (status_from_flags(fl, false) != NS_OK) {
         a.out_ids[row] = status_from_flags(fl, false);
       }
     }
     __syncthreads();
     if (mode == MODE_FAST && status_from_flags(m->flags, false) == NS_OK) {
-      if (m->roff[CL * kWarps] <= kRankMax)
+      if (m->roff[CL * kWarps] <= kRankMax) {
         gather_keys(c, cluster, CL);
-      else
+      } else if (a.vp_keys) {
+        if (tid == 0) a.out_ids[row] = NS_ERR_CANDIDATE_OVERFLOW;
+      } else {
         leader_gather(c, a, cluster, CL);
+      }
     }
   }
   cluster.sync();
   if (rank == 0 && mode == MODE_FAST && status_from_flags(m->flags, false) == NS_OK) {
     if (m->roff[CL * kWarps] <= kRankMax)
       rank_finalize(c, a, row, topp, m->roff[CL * kWarps]);
-    else
+    else if (!a.vp_keys)
       finalize_row(c, a, row, topp);
   }
+}
+
+// ---------------------------------------------------------------------------
+// vocab-parallel merge: one CTA per row over the all-gathered records of
+// n_ranks column slices.  Record of rank r (int64): [batch] counts or
+// statuses, then [batch][cap] keys (f2key(y) << 32 | ~global id).  Every
+// element of the row's global top-k (with ties at the k-th scaled value)
+// lies in its own slice's top-k with ties, so the union holds the global set
+// and the result equals the single-device call on the whole row.
+// ---------------------------------------------------------------------------
+constexpr int kMergeStage = kMergeCap;  // union keys the merge stages (32 KB at the stage area's start)
+static_assert(size_t(kMergeStage) * 8 <= kRankKeysOff, "staged lists end before the sorted keys");
+
+struct VpMerge {
+  const int64_t* rec;
+  int n_ranks;
+  int cap;
+  int64_t batch;
+};
+
+__device__ __forceinline__ int status_rank(int64_t st) {  // single-device priority order
+  switch (int(st)) {
+    case NS_ERR_DEVICE_TIMEOUT: return 0;
+    case NS_ERR_TOKEN_ID_OUT_OF_RANGE: return 1;
+    case NS_ERR_HISTORY_TOO_LONG: return 2;
+    case NS_ERR_UNSUPPORTED: return 3;
+    case NS_ERR_INVALID_DISTRIBUTION: return 4;
+    case NS_ERR_CANDIDATE_OVERFLOW: return 5;
+    default: return 6;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) vp_merge_kernel(const __grid_constant__ KArgs a,
+                                                            const __grid_constant__ VpMerge v) {
+  using C_ = Ctx<NS_DTYPE_F32>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int64_t row = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  C_ c;
+  c.stages = smem;
+  c.m = reinterpret_cast<Misc*>(smem + kStageBytes);
+  c.row = row;
+  const float T = a.temperature[row];
+  const int topk = a.top_k[row];
+  const float topp = a.top_p[row];
+  c.K = topk;
+  c.Tabs = fabsf(T);
+  c.neg = T < 0.0f;
+  c.u_pre = a.uniforms ? a.uniforms[row] : 0.0f;
+  Misc* m = c.m;
+  const int64_t rlen = v.batch * (1 + int64_t(v.cap));
+  if (tid == 0) {
+    int64_t err = 0;
+    int tot = 0;
+    for (int r = 0; r < v.n_ranks; ++r) {
+      const int64_t h = v.rec[r * rlen + row];
+      m->roff[r] = tot;
+      if (h < 0) {
+        if (err == 0 || status_rank(h) < status_rank(err)) err = h;
+      } else {
+        tot += int(h < int64_t(v.cap) ? h : int64_t(v.cap));
+      }
+    }
+    m->roff[v.n_ranks] = tot;
+    m->flags = int(err);
+  }
+  __syncthreads();
+  if (m->flags != 0) {
+    if (tid == 0) a.out_ids[row] = m->flags;
+    return;
+  }
+  if (T == 0.0f) {  // greedy: the largest key over the ranks
+    if (warp == 0) {
+      uint64_t best = 0;
+      for (int r = lane; r < v.n_ranks; r += 32) {
+        const int64_t* base = v.rec + r * rlen;
+        if (base[row] > 0) best = max(best, uint64_t(base[v.batch + row * v.cap]));
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) best = max(best, __shfl_xor_sync(kFull, best, o));
+      if (lane == 0) a.out_ids[row] = best ? int64_t(~uint32_t(best)) : NS_ERR_INVALID_DISTRIBUTION;
+    }
+    return;
+  }
+  if (!(topk > 0 && int64_t(topk) < a.vocab_total && topk <= kFastK)) {
+    if (tid == 0) a.out_ids[row] = NS_ERR_UNSUPPORTED;
+    return;
+  }
+  // Each rank's keys arrive sorted (descending) and distinct across ranks, so a
+  // key's position in the union is its index in its own list plus, for every
+  // other list, the number of keys above it.  The lists are staged in shared
+  // memory; keys placed past kRankMax cannot be among the kept ones unless a
+  // tie run reaches them (finalize_keys reports that as overflow).
+  const int n = m->roff[v.n_ranks];
+  if (n > kMergeStage) {
+    if (tid == 0) a.out_ids[row] = NS_ERR_CANDIDATE_OVERFLOW;
+    return;
+  }
+  uint64_t* lists = reinterpret_cast<uint64_t*>(c.stages);
+  uint64_t* sorted = reinterpret_cast<uint64_t*>(c.stages + kRankKeysOff) + kRankMax;
+  for (int r = warp; r < v.n_ranks; r += kWarps) {
+    const int cnt = m->roff[r + 1] - m->roff[r];
+    const int64_t* src = v.rec + r * rlen + v.batch + row * v.cap;
+    for (int i = lane; i < cnt; i += 32) lists[m->roff[r] + i] = uint64_t(src[i]);
+  }
+  __syncthreads();
+  for (int e = tid; e < n; e += kThreads) {
+    int r = 0;
+    while (m->roff[r + 1] <= e) ++r;
+    const uint64_t key = lists[e];
+    int pos = e - m->roff[r];
+    for (int r2 = 0; r2 < v.n_ranks; ++r2) {
+      if (r2 == r) continue;
+      const uint64_t* l2 = lists + m->roff[r2];
+      int lo = 0, hi = m->roff[r2 + 1] - m->roff[r2];
+      while (lo < hi) {  // keys of list r2 above `key`
+        const int mid = (lo + hi) >> 1;
+        if (l2[mid] > key)
+          lo = mid + 1;
+        else
+          hi = mid;
+      }
+      pos += lo;
+    }
+    if (pos < kRankMax) sorted[pos] = key;
+  }
+  __syncthreads();
+  finalize_keys(c, a, row, topp, min(n, kRankMax), n);
 }
 
 // ---------------------------------------------------------------------------
@@ -2555,6 +2741,25 @@ static int launch(const KArgs& base, int64_t batch, ns_stream_t stream) {
   return NS_OK;
 }
 
+static int vp_merge_launch(const KArgs& a, const VpMerge& v, ns_stream_t stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return NS_ERR_CUDA;
+  const size_t smem_bytes = kStageBytes + sizeof(Misc);
+  {
+    static bool configured[64] = {};
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!configured[dev]) {
+      if (cudaFuncSetAttribute(vp_merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem_bytes)) !=
+          cudaSuccess)
+        return NS_ERR_CUDA;
+      configured[dev] = true;
+    }
+  }
+  vp_merge_kernel<<<unsigned(v.batch), kThreads, smem_bytes, reinterpret_cast<cudaStream_t>(stream)>>>(a, v);
+  if (cudaGetLastError() != cudaSuccess) return NS_ERR_CUDA;
+  return NS_OK;
+}
+
 }  // namespace ns
 
 // ---------------------------------------------------------------------------
@@ -2626,6 +2831,78 @@ int ns_sample(const void* logits, int dtype, int64_t batch, int64_t vocab, int64
     case NS_DTYPE_BF16: return ns::launch<NS_DTYPE_BF16>(a, batch, stream);
     default: return ns::launch<NS_DTYPE_F16>(a, batch, stream);
   }
+}
+
+int ns_vp_record_int64s(int64_t batch, int cap, int64_t* out_count) {
+  if (!out_count || batch < 0 || cap < 1 || cap > ns::kRankMax) return NS_ERR_INVALID_ARGUMENT;
+  *out_count = batch * (1 + int64_t(cap));
+  return NS_OK;
+}
+
+int ns_vp_local(const void* logits, int dtype, int64_t batch, int64_t vocab_local, int64_t row_stride,
+                int64_t vocab_offset, int64_t vocab_total, const int32_t* hist_ids, const int64_t* hist_offsets,
+                int64_t max_history, const float* temperature, const int32_t* top_k, const float* top_p,
+                const float* repetition_penalty, const float* presence_penalty, const float* frequency_penalty,
+                int cap, int64_t* record, ns_stream_t stream) {
+  if (dtype != NS_DTYPE_F32 && dtype != NS_DTYPE_BF16 && dtype != NS_DTYPE_F16) return NS_ERR_UNSUPPORTED_DTYPE;
+  if (batch < 0 || vocab_local <= 0 || row_stride < vocab_local || max_history < 0) return NS_ERR_INVALID_ARGUMENT;
+  if (vocab_offset < 0 || vocab_total < vocab_offset + vocab_local || vocab_total > (int64_t(1) << 24) ||
+      batch > (int64_t(1) << 24))
+    return NS_ERR_INVALID_ARGUMENT;
+  if (cap < 1 || cap > ns::kRankMax) return NS_ERR_INVALID_ARGUMENT;
+  if ((hist_ids == nullptr) != (hist_offsets == nullptr)) return NS_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return NS_OK;
+  if (!logits || !temperature || !top_k || !top_p || !record) return NS_ERR_INVALID_ARGUMENT;
+  ns::KArgs a = {};
+  a.logits = logits;
+  a.vocab = vocab_local;
+  a.row_stride = row_stride;
+  a.vocab_offset = vocab_offset;
+  a.vocab_total = vocab_total;
+  a.hist_ids = hist_ids;
+  a.hist_offsets = hist_offsets;
+  a.max_history = max_history;
+  a.temperature = temperature;
+  a.top_k = top_k;
+  a.top_p = top_p;
+  a.rep = repetition_penalty;
+  a.pres = presence_penalty;
+  a.freq = frequency_penalty;
+  a.out_ids = record;           // [batch] counts / statuses
+  a.vp_keys = record + batch;   // [batch][cap] keys
+  a.vp_cap = cap;
+  switch (dtype) {
+    case NS_DTYPE_F32: return ns::launch<NS_DTYPE_F32>(a, batch, stream);
+    case NS_DTYPE_BF16: return ns::launch<NS_DTYPE_BF16>(a, batch, stream);
+    default: return ns::launch<NS_DTYPE_F16>(a, batch, stream);
+  }
+}
+
+int ns_vp_merge(const int64_t* gathered, int n_ranks, int64_t batch, int cap, int64_t vocab_total,
+                const float* temperature, const int32_t* top_k, const float* top_p, const float* uniforms,
+                uint64_t philox_seed, uint64_t philox_offset, int64_t* out_ids, ns_stream_t stream) {
+  if (n_ranks < 1 || n_ranks > ns::kMaxLists || batch < 0 || cap < 1 || cap > ns::kRankMax) return NS_ERR_INVALID_ARGUMENT;
+  if (vocab_total <= 0 || vocab_total > (int64_t(1) << 24) || batch > (int64_t(1) << 24)) return NS_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return NS_OK;
+  if (!gathered || !temperature || !top_k || !top_p || !out_ids) return NS_ERR_INVALID_ARGUMENT;
+  ns::KArgs a = {};
+  a.vocab = vocab_total;
+  a.vocab_offset = 0;
+  a.vocab_total = vocab_total;
+  a.temperature = temperature;
+  a.top_k = top_k;
+  a.top_p = top_p;
+  a.uniforms = uniforms;
+  a.seed = philox_seed;
+  a.offset = philox_offset;
+  a.out_ids = out_ids;
+  a.merge_cap = ns::kMergeCap;
+  ns::VpMerge v;
+  v.rec = gathered;
+  v.n_ranks = n_ranks;
+  v.cap = cap;
+  v.batch = batch;
+  return ns::vp_merge_launch(a, v, stream);
 }
 
 }  // extern "C"
