@@ -339,6 +339,108 @@ def run_ours(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_vp(args, world, rank, local):
+    """vocab-parallel sampling, B=128 rows of V=151936 fp32
+    split into `world` contiguous slices; per step ns_vp_local on this rank's
+    slice, an all-gather of the candidate records (NCCL), ns_vp_merge.  Total
+    work is fixed as N grows (strong scaling); tokens/s counts the B rows once."""
+    import ctypes
+    import torch.distributed as dist
+    from b200_sampler import _lib
+    from b200_sampler.params import SamplingParams, pack_params
+    from b200_sampler.vocab_parallel import gather_records
+    from b200_sampler.workloads import make_logits, make_uniforms
+
+    dev = torch.device("cuda", local)
+    B, V, K = 128, 151936, 50
+    w = (V + world - 1) // world
+    off = rank * w
+    width = min(w, V - off)
+    full = make_logits(0, B, V, 3.0)
+    bufs = [full[:, off:off + width].contiguous().to(dev)]
+    for i in range(1, N_BUFFERS):
+        bufs.append(full.roll(i, dims=1)[:, off:off + width].contiguous().to(dev))
+    params = [SamplingParams(temperature=0.8, top_k=K, top_p=0.95)] * B
+    p = torch.from_numpy(pack_params(params)).to(dev)
+    pp = p.data_ptr()
+    u = make_uniforms(1, B).to(dev)
+    cap = K + 16
+    n = ctypes.c_int64()
+    lib = _lib.load()
+    assert lib.ns_vp_record_int64s(B, cap, ctypes.byref(n)) == 0
+    rec = torch.empty(n.value, dtype=torch.int64, device=dev)
+    out = torch.empty(B, dtype=torch.int64, device=dev)
+    side = torch.cuda.Stream(dev)
+
+    def step(i):
+        x = bufs[i % N_BUFFERS]
+        rc = lib.ns_vp_local(x.data_ptr(), _lib.NS_DTYPE_F32, B, width, width, off, V, None, None, 0,
+                             pp, pp + 4 * B, pp + 8 * B, None, None, None, cap, rec.data_ptr(), side.cuda_stream)
+        assert rc == 0
+        g = gather_records(rec) if world > 1 else rec
+        rc = lib.ns_vp_merge(g.data_ptr(), world, B, cap, V, pp, pp + 4 * B, pp + 8 * B, u.data_ptr(), 0, 0,
+                             out.data_ptr(), side.cuda_stream)
+        assert rc == 0
+
+    with torch.cuda.stream(side):
+        for i in range(max(args.warmup, 3)):
+            step(i)
+    torch.cuda.synchronize(dev)
+    assert int(out.min()) >= 0
+
+    # CUDA graphs of up to 100 steps (every rank captures the same collectives)
+    per = min(args.steps, 100)
+    reps, rem = divmod(args.steps, per)
+
+    def capture(nsteps):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            for i in range(nsteps):
+                step(i)
+        return g
+    g = capture(per)
+    g_rem = capture(rem) if rem else None
+    with torch.cuda.stream(side):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clk:
+        with torch.cuda.stream(side):
+            e0.record(side)
+            for _ in range(reps):
+                g.replay()
+            if g_rem is not None:
+                g_rem.replay()
+            e1.record(side)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    del g, g_rem  # graphs holding NCCL calls go before the process group
+    ms = max_over_ranks(world, e0.elapsed_time(e1))
+    ms_per_step = ms / args.steps
+    peak, peak_kind = _peaks()
+    local_bytes = B * width * 4
+    line = {"metric": "vocab-parallel sampled tokens/sec at B=128,V=151936 (BASELINE config 4)",
+            "value": B / (ms_per_step / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded randn*3 logits)",
+            "config": {"workload": f"B={B} V={V} fp32 split into {world} slices of <= {w}; T=0.8 k={K} p=0.95",
+                       "record_bytes_per_rank": int(n.value) * 8,
+                       "timing": f"CUDA graphs of local + NCCL all-gather + merge ({per} steps x {reps}"
+                                 f"{f' + {rem}' if rem else ''}), CUDA events, max over ranks"},
+            "roofline": {"bound": "hbm", "achieved": local_bytes / (ms_per_step / 1e3) / 1e9, "peak": peak,
+                         "unit": "GB/s", "frac": local_bytes / (ms_per_step / 1e3) / 1e9 / peak,
+                         "traffic": None, "peak_kind": peak_kind, "algorithmic_bytes_per_launch": local_bytes},
+            "gpu_launches": 2 * args.steps}
+    clocks = clk.summary()
+    if clocks is not None:
+        line["clocks"] = clocks
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -347,6 +449,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
+    ap.add_argument("--mode", default="rows", choices=["rows", "vp"],
+                    help="rows: the headline (rows sharded); vp: vocab-parallel config 4")
     args = ap.parse_args()
     world, rank, local = (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
                           int(os.environ.get("LOCAL_RANK", "0")))
@@ -355,7 +459,10 @@ def main():
         return
     world, rank, local = dist_setup(args.gpus)
     try:
-        run_ours(args, world, rank, local)
+        if args.mode == "vp":
+            run_vp(args, world, rank, local)
+        else:
+            run_ours(args, world, rank, local)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -23,6 +23,7 @@ Differences from the reference, all documented in the C header:
 """
 from __future__ import annotations
 
+import array
 import itertools
 import threading
 from typing import List, Optional, Sequence
@@ -217,11 +218,16 @@ class B200Sampler(SamplerBase):
             offs = h[off_offsets:off_offsets + (B + 1) * 8].view(np.int64)
             offs[0] = 0
             np.cumsum(lens, out=offs[1:])
-            flat = np.fromiter(itertools.chain.from_iterable(all_generated_ids), dtype=np.int64,
-                               count=total)
-            if flat.min() < -(2 ** 31) or flat.max() >= 2 ** 31:
-                raise IndexError(_lib.status_string(_lib.NS_ERR_TOKEN_ID_OUT_OF_RANGE))
-            h[off_ids:off_ids + total * 4].view(np.int32)[:] = flat
+            ids32 = h[off_ids:off_ids + total * 4].view(np.int32)
+            pos = 0
+            try:  # one C-level conversion per row (ids beyond int32 cannot be token ids)
+                for row in all_generated_ids:
+                    n = len(row)
+                    if n:
+                        ids32[pos:pos + n] = np.frombuffer(array.array("i", row), dtype=np.int32)
+                        pos += n
+            except OverflowError:
+                raise IndexError(_lib.status_string(_lib.NS_ERR_TOKEN_ID_OUT_OF_RANGE)) from None
         if host_u:
             hu = uniforms.detach().to(torch.float32).reshape(-1).numpy()
             if hu.size != B:
