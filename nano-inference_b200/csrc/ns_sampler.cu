@@ -1354,6 +1354,8 @@ __device__ __forceinline__ bool block_kth_regs(Misc* m, const uint32_t (&key)[R]
 // barrier; rank_finalize sorts it by counting, for each key, the keys above
 // it, and takes the top-k with its ties at the k-th scaled value.
 constexpr int kRankMax = 1024;
+static_assert(kRankMax * 8 <= kCandBytes, "sorted keys of a single-CTA row fit the candidate buffers");
+static_assert((kCapW + 1) * 8 <= kWStageStride, "a warp's keys (padded) fit its first stage");
 // keys[kRankMax] and sorted[kRankMax] in the stage area, past the merge lists
 // (y, id: kMergeCap * 8 bytes), finalize_small's arrays (5 * kSmallN * 4) and
 // finalize_row's sort keys for up to kRankMax survivors
@@ -1383,7 +1385,8 @@ __device__ __forceinline__ void gather_keys(const Ctx<DT>& c, cg::cluster_group&
 }
 
 template <int DT>
-__device__ void finalize_keys(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, int n, int n_all);
+__device__ void finalize_keys(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, const uint64_t* sorted,
+                              int n, int n_all);
 
 template <int DT>
 __device__ void rank_finalize(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, int n) {
@@ -1406,18 +1409,19 @@ __device__ void rank_finalize(const Ctx<DT>& c, const KArgs& a, int64_t row, flo
     sorted[r0 + r1] = ki;
   }
   __syncthreads();
-  finalize_keys(c, a, row, topp, n, n);
+  finalize_keys(c, a, row, topp, sorted, n, n);
 }
 
-// The first n keys of the sorted union (descending) are in sorted[]; n_all >=
+// The first n keys of the sorted union (descending) are in sorted[] (outside
+// the first 32 KB + 2.5 KB of the stage area, which the finalise reuses); n_all >=
 // n survivors exist in total.  Top-k keeps every key whose scaled value ties
 // the k-th (reference sampler.py:116-121); each warp finds the end of the tie
 // run itself.  A tie run that reaches past the n placed keys overflows.
 template <int DT>
-__device__ void finalize_keys(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, int n, int n_all) {
+__device__ void finalize_keys(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, const uint64_t* sorted,
+                              int n, int n_all) {
   Misc* m = c.m;
   const int tid = threadIdx.x, lane = tid & 31;
-  uint64_t* sorted = reinterpret_cast<uint64_t*>(c.stages + kRankKeysOff) + kRankMax;
   if (n == 0) {  // nothing finite (a vocab-parallel slice may legitimately hold none)
     if (tid == 0) a.out_ids[row] = a.vp_keys ? 0 : NS_ERR_INVALID_DISTRIBUTION;
     return;
@@ -1470,6 +1474,105 @@ __device__ void finalize_keys(const Ctx<DT>& c, const KArgs& a, int64_t row, flo
   if (tid == 0) m->n_merge = nfin;
   __syncthreads();
   finalize_row(c, a, row, topp);
+}
+
+// Rows on one CTA (cluster size 1), GREEDY and FAST: the end of the row with
+// few block barriers.  FAST: after every warp published its final bound, each
+// warp turns its survivors of the tightest bound into keys
+// (f2key(x / T) << 32) | ~id in its own stage bytes (its copies are all
+// consumed); after one barrier each warp places its keys in the union by
+// counting the keys above them in all eight lists, into the candidate buffers
+// (no longer read), and finalize_keys takes the top-k with ties.  Returns
+// false (the same on every thread) when the row continues on the general
+// merge below: tied values that overflowed a buffer (multi-pass path) or a
+// union of more than kRankMax survivors (radix-select merge).
+template <int DT>
+__device__ bool single_block_tail(const Ctx<DT>& c, const KArgs& a, int mode, bool ok, const WarpCand& s, float best,
+                                  int bidx, float topp) {
+  Misc* m = c.m;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t row = c.row;
+  if (mode == MODE_GREEDY) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ob = __shfl_xor_sync(kFull, best, o);
+      const int oi = __shfl_xor_sync(kFull, bidx, o);
+      if (better(ob, oi, best, bidx)) {
+        best = ob;
+        bidx = oi;
+      }
+    }
+    if (lane == 0) {
+      m->wbest[warp] = best;
+      m->widx[warp] = bidx;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float b = m->wbest[0];
+      int bi = m->widx[0];
+      for (int w = 1; w < kWarps; ++w)
+        if (better(m->wbest[w], m->widx[w], b, bi)) {
+          b = m->wbest[w];
+          bi = m->widx[w];
+        }
+      const int st = status_from_flags(m->flags, true);
+      a.out_ids[row] = (st != NS_OK) ? int64_t(st) : int64_t(bi) + a.vocab_offset;
+    }
+    return true;
+  }
+  // every warp's final bound, then only survivors of the tightest become keys
+  if (ok) publish_bound(c, s);
+  __syncthreads();
+  WarpCand f = s;
+  read_shared_tau(c, f);
+  uint64_t* keys = reinterpret_cast<uint64_t*>(c.stage(warp, 0));
+  int nw = 0;
+  if (ok && !s.ovf) {
+    for (int i0 = 0; i0 < s.n; i0 += 32) {
+      const int i = i0 + lane;
+      const bool keep = i < s.n && s.x[i] >= f.tau;
+      const unsigned mk = __ballot_sync(kFull, keep);
+      if (keep) {
+        const float y = __fdiv_rn(s.x[i], c.Tabs) + 0.0f;  // -0 and +0 tie
+        keys[nw + __popc(mk & lanemask_lt())] = (uint64_t(f2key(y)) << 32) | uint64_t(~uint32_t(c.c0 + s.col[i]));
+      }
+      nw += __popc(mk);
+    }
+  }
+  if (lane == 0) {
+    if (nw & 1) keys[nw] = 0ull;  // pad to whole pairs
+    m->wn[warp] = nw;
+  }
+  __syncthreads();
+  const int fl = m->flags;
+  if ((fl & F_OVF) && !(fl & (F_NAN | F_TIMEOUT | F_BADID | F_HIST))) return false;
+  const int st = status_from_flags(fl, false);
+  if (st != NS_OK) {
+    if (tid == 0) a.out_ids[row] = st;
+    return true;
+  }
+  int n = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) n += m->wn[w];
+  if (n > kRankMax) return false;  // a union this large takes the radix-select merge
+  uint64_t* sorted = reinterpret_cast<uint64_t*>(c.cx);
+  for (int i = lane; i < nw; i += 32) {
+    const uint64_t ki = keys[i];
+    int pos = 0;
+    for (int w2 = 0; w2 < kWarps; ++w2) {
+      const uint64_t* k2 = reinterpret_cast<const uint64_t*>(c.stage(w2, 0));
+      const int n2 = m->wn[w2];
+#pragma unroll 4
+      for (int j = 0; j < n2; j += 2) {
+        const ulonglong2 p = *reinterpret_cast<const ulonglong2*>(k2 + j);
+        pos += ((p.x > ki) ? 1 : 0) + ((p.y > ki) ? 1 : 0);
+      }
+    }
+    if (pos < kRankMax) sorted[pos] = ki;
+  }
+  __syncthreads();
+  finalize_keys(c, a, row, topp, sorted, n, n);
+  return true;
 }
 
 // Leader, FAST rows: the K-th largest value over the union of every warp list
@@ -2375,6 +2478,10 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     }
   }
   if (mode == MODE_FAST && s.ovf && lane == 0) atomicOr(&m->flags, F_OVF);
+  if (CL == 1 && mode != MODE_GENERAL && !a.vp_keys) {
+    if (single_block_tail(c, a, mode, ok, s, best, bidx, topp)) return;
+    __syncthreads();  // the row continues on the general merge below
+  }
   if (mode == MODE_FAST) {  // every warp's final bound; survivors of the tightest
     if (ok) publish_bound(c, s);
     __syncthreads();
@@ -2618,7 +2725,7 @@ __global__ void __launch_bounds__(kThreads) vp_merge_kernel(const __grid_constan
     if (pos < kRankMax) sorted[pos] = key;
   }
   __syncthreads();
-  finalize_keys(c, a, row, topp, min(n, kRankMax), n);
+  finalize_keys(c, a, row, topp, sorted, min(n, kRankMax), n);
 }
 
 // ---------------------------------------------------------------------------
