@@ -287,6 +287,17 @@ __device__ float scaled_lower_bound(float xk, float T) {
   return key2f(hi);
 }
 
+// A filter bound at or below scaled_lower_bound(xk, T) without divisions: if
+// x <= xk - |xk| 2^-21 then x / T lies below xk / T by more than two relative
+// rounding errors (2^-24 each in the normal range), so rn(x / T) <
+// rn(xk / T).  xk - |xk| 2^-20 is below that even after its own rounding.
+// Magnitudes where x / T could leave the normal range use the exact search.
+__device__ __forceinline__ float fast_lower_bound(float xk, float T) {
+  const float a = fabsf(xk);
+  if (a >= 0x1p-60f && a <= 0x1p60f && T >= 0x1p-30f && T <= 0x1p30f) return fmaf(-a, 0x1p-20f, xk);
+  return scaled_lower_bound(xk, T);
+}
+
 // ---------------------------------------------------------------------------
 // per-warp candidate buffer (warp-uniform state)
 // ---------------------------------------------------------------------------
@@ -331,7 +342,7 @@ __device__ void warp_compact(const Ctx<DT>& c, WarpCand& s) {
   if (s.n > c.K) {
     const uint32_t kk = warp_kth_key(key, c.K);
     float t = 0.0f;
-    if (lane == 0) t = scaled_lower_bound(key2f(kk), c.Tabs);
+    if (lane == 0) t = fast_lower_bound(key2f(kk), c.Tabs);
     s.tau = fmaxf(s.tau, __shfl_sync(kFull, t, 0));
   }
   int base = 0;
@@ -850,10 +861,10 @@ __device__ __forceinline__ float tile_lane_max(const Ctx<DT>& c, int w, int t, c
 // element of the warp's columns >= its own tau is held, so v_w has kq elements
 // of the CTA at or above it.  Once all kWarps warps have published, the CTA has
 // at least kWarps * kq >= K elements >= min_w v_w: a lower bound of its K-th
-// largest.  The published value is already the collision-safe filter bound
-// scaled_lower_bound(v_w), which is monotone in v_w, so the minimum of the
-// published bounds is the bound of min_w v_w.  Published values only grow, so
-// a stale read is still valid.
+// largest.  The published value is already a filter bound b_w <=
+// scaled_lower_bound(v_w) (fast_lower_bound), so the minimum of the published
+// bounds is at most the bound of the smallest v_w, which is a valid filter for
+// the CTA.  Published values only grow, so a stale read is still valid.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ int share_kq(int K) { return (K + kWarps - 1) / kWarps; }
 
@@ -885,7 +896,7 @@ template <int DT>
 __device__ __forceinline__ void publish_key(const Ctx<DT>& c, uint32_t v) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0 && v != 0u) {
-    const uint32_t b = f2key(scaled_lower_bound(key2f(v), c.Tabs));
+    const uint32_t b = f2key(fast_lower_bound(key2f(v), c.Tabs));
     volatile uint32_t* pub = c.m->pub;
     if (b > pub[warp]) pub[warp] = b;
   }
