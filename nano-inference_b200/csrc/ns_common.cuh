@@ -143,6 +143,14 @@ __device__ __forceinline__ float fmax_nan(float a, float b) {
   return d;
 }
 
+// 2^a by the hardware approximation (PTX ex2.approx.ftz.f32: relative error
+// about 2^-22; results below 2^-126 flush to zero).
+__device__ __forceinline__ float ex2_approx(float a) {
+  float d;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(d) : "f"(a));
+  return d;
+}
+
 // min that propagates NaN (PTX min.NaN, sm_80+).
 __device__ __forceinline__ float fmin_nan(float a, float b) {
   float d;

@@ -74,7 +74,7 @@ static_assert(kMergeCap * 16 <= kStageBytes, "merge lists and their sort keys fi
 constexpr int kMaxLists = kMaxCluster * kWarps;
 constexpr unsigned kFull = 0xFFFFFFFFu;
 
-enum : int { MODE_GREEDY = 0, MODE_FAST = 1, MODE_GENERAL = 2 };
+enum : int { MODE_GREEDY = 0, MODE_FAST = 1, MODE_GENERAL = 2, MODE_SOFTMAX = 3 };
 enum : int { F_NAN = 1, F_BADID = 2, F_HIST = 4, F_OVF = 8, F_TIMEOUT = 16, F_UNSUP = 32 };
 
 // ---------------------------------------------------------------------------
@@ -131,6 +131,8 @@ struct Misc {
   unsigned long long g_tbefore; // ... and the kept mass before it
   int segoff[kWarps + 1];   // distinct history ids before each warp's columns
   uint32_t pub[kWarps];     // FAST: per-warp published bound (key; 0 = none)
+  double s_rem;             // SOFTMAX: the draw's remaining mass inside the chosen warp
+  int s_warp;               // ... and that warp
   int roff[kMaxLists + 1];  // leader: union offsets over (rank, warp) lists
   int rc0[kMaxCluster];     // leader: first column of each rank
   uint32_t hist[kBins];
@@ -856,6 +858,116 @@ __device__ __forceinline__ float tile_lane_max(const Ctx<DT>& c, int w, int t, c
 }
 
 // ---------------------------------------------------------------------------
+// SOFTMAX rows (top-k and top-p both off): one pass.  Per warp tile, the
+// largest scaled value ym = rn(xmax / |T|) and D = sum of expf(rn(x / |T|) - ym)
+// over its finite values, in float64; the draw is located afterwards from the
+// tiles' masses scaled by expf(ym - M) and one tile is read again.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ double* softmax_tile_mass(void* tacc) { return reinterpret_cast<double*>(tacc); }
+template <int DT>
+__device__ __forceinline__ float* softmax_tile_max(const Ctx<DT>& c) {
+  return reinterpret_cast<float*>(softmax_tile_mass(c.tacc) + kWarps * c.tpw);
+}
+
+// x / T within one ulp from r = rn(1 / T): the product's remainder, exact by
+// FMA, corrects the quotient once (Newton-Raphson; Markstein, IBM J. Res.
+// Dev. 34(1), 1990).  A quotient that overflows comes out NaN or infinite.
+__device__ __forceinline__ float quot_nr(float x, float T, float r) {
+  const float q = x * r;
+  return fmaf(fmaf(-q, T, x), r, q);
+}
+
+// exp(d) for d <= ~0 as 2^(d log2 e), the product kept as hi + lo: log2 e is
+// split into two fp32 parts (Cody and Waite's two-constant reduction), hi =
+// rn(d L1), lo = the product's rounding error (FMA) plus d L2.  2^hi by the
+// hardware approximation, the lo term to first order: relative error ~2^-22.
+__device__ __forceinline__ float exp_split(float d) {
+  constexpr float L1 = 1.4426950216293335f;       // fp32 nearest to log2(e)
+  constexpr float L2 = 1.925963033500011e-08f;    // log2(e) - L1
+  constexpr float LN2 = 0.693147182464599609375f;
+  const float hi = d * L1;
+  const float lo = fmaf(d, L2, fmaf(d, L1, -hi));
+  const float p = ex2_approx(hi);
+  return fmaf(p * lo, LN2, p);
+}
+
+// Softmax weight of a value x (filter domain) in a tile whose largest scaled
+// value is ym: exp(x / |T| - ym).  A quotient that overflows (NaN or -inf)
+// clamps to weight 0; a tile whose own maximum overflows reports the row
+// instead, so no value above ym can overflow.
+__device__ __forceinline__ float softmax_weight(float x, float ym, float T, float r) {
+  return exp_split(fmaxf(quot_nr(x, T, r) - ym, -1000.0f));
+}
+
+// SOFTMAX per-tile mass.  FULL: every slot is a column and slot 0 is column 0.
+template <int DT, bool NEG, bool FULL>
+__device__ __forceinline__ void mass_tile_t(const Ctx<DT>& c, int w, int t, const uint8_t* st) {
+  constexpr int VE = Ctx<DT>::VE;
+  const int lane = threadIdx.x & 31;
+  const int len = FULL ? Ctx<DT>::TE : c.tile_len(w, t), lead = FULL ? 0 : c.tile_lead(w, t);
+  const int n_groups = (lead + len + VE - 1) / VE;
+  float mx = -INFINITY;  // NaN-propagating: NaN or +inf anywhere shows here
+  for (int q = lane; q < n_groups; q += 32) {
+    const uint4 v = *reinterpret_cast<const uint4*>(st + q * 16);
+    if (FULL) {
+      mx = fmax_nan(mx, group_extreme<DT, NEG>(v));
+    } else {
+      float x[VE];
+      unpack16<DT>(v, x);
+#pragma unroll
+      for (int i = 0; i < VE; ++i)
+        if (q * VE + i >= lead && q * VE + i < lead + len) mx = fmax_nan(mx, NEG ? -x[i] : x[i]);
+    }
+  }
+  float ym = -INFINITY;
+  double acc = 0.0;
+  if (__any_sync(kFull, !(mx < INFINITY))) {
+    if (lane == 0) atomicOr(&c.m->flags, F_NAN);
+  } else {
+    const float xm = key2f(__reduce_max_sync(kFull, f2key(mx)));
+    if (xm > -INFINITY) {
+      ym = __fdiv_rn(xm, c.Tabs);
+      if (!(ym < INFINITY)) {  // x / T overflows: the reference's softmax is NaN
+        if (lane == 0) atomicOr(&c.m->flags, F_NAN);
+        ym = -INFINITY;
+      } else {
+        // a 16-byte group's weights summed pairwise in fp32, then in float64
+        const float rT = __frcp_rn(c.Tabs);
+        for (int q = lane; q < n_groups; q += 32) {
+          float x[VE];
+          unpack16<DT>(*reinterpret_cast<const uint4*>(st + q * 16), x);
+          float wv[VE];
+#pragma unroll
+          for (int i = 0; i < VE; ++i) {
+            const bool in = FULL || (q * VE + i >= lead && q * VE + i < lead + len);
+            wv[i] = in ? softmax_weight(NEG ? -x[i] : x[i], ym, c.Tabs, rT) : 0.0f;
+          }
+#pragma unroll
+          for (int h = VE / 2; h >= 1; h >>= 1)
+#pragma unroll
+            for (int i = 0; i < h; ++i) wv[i] += wv[i + h];
+          acc += double(wv[0]);
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
+      }
+    }
+  }
+  if (lane == 0) {
+    softmax_tile_mass(c.tacc)[w * c.tpw + t] = acc;
+    softmax_tile_max(c)[w * c.tpw + t] = ym;
+  }
+}
+
+template <int DT, bool NEG>
+__device__ __forceinline__ void mass_tile(const Ctx<DT>& c, int w, int t, const uint8_t* st, bool full) {
+  if (full)
+    mass_tile_t<DT, NEG, true>(c, w, t, st);
+  else
+    mass_tile_t<DT, NEG, false>(c, w, t, st);
+}
+
+// ---------------------------------------------------------------------------
 // FAST threshold sharing without block barriers.  A warp publishes a bound
 // from v_w, the kq-th largest (kq = ceil(K / kWarps)) element it holds; every
 // element of the warp's columns >= its own tau is held, so v_w has kq elements
@@ -949,6 +1061,11 @@ __device__ __forceinline__ bool stream_warp(const Ctx<DT>& c, int mode, uint64_t
     }
     if (mode == MODE_GREEDY) {
       greedy_tile(c, w, t, st, best, bidx, t < nfull);
+    } else if (mode == MODE_SOFTMAX) {
+      if (c.neg)
+        mass_tile<DT, true>(c, w, t, st, t < nfull);
+      else
+        mass_tile<DT, false>(c, w, t, st, t < nfull);
     } else if (!s.ovf) {
       if (c.neg)
         fast_tile<DT, true>(c, s, w, t, st, t < nfull);
@@ -1584,6 +1701,182 @@ __device__ bool single_block_tail(const Ctx<DT>& c, const KArgs& a, int mode, bo
   __syncthreads();
   finalize_keys(c, a, row, topp, sorted, n, n);
   return true;
+}
+
+// SOFTMAX rows on one CTA: after the stream (tile masses in place, penalised
+// history values computed), locate the draw u * Z in column order -- warp,
+// then tile -- and read that tile again to find the id.  Weights are
+// expf(rn(x / |T|) - ym_t) * expf(ym_t - M) for the tiles' values and
+// expf(rn(xp / |T|) - M) for history columns (penalised xp), summed in float64
+// in the same way for the totals and for the final scan.
+template <int DT>
+__device__ void softmax_tail(const Ctx<DT>& c, const KArgs& a, uint64_t policy) {
+  using E = Elem<DT>;
+  using R = typename E::raw;
+  constexpr int TE = Ctx<DT>::TE;
+  Misc* m = c.m;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t row = c.row;
+  const double* tD = softmax_tile_mass(c.tacc);
+  const float* tY = softmax_tile_max(c);
+  const int nt = c.wtiles(warp);
+  const int hr0 = c.pen ? m->segoff[warp] : 0, hr1 = c.pen ? m->segoff[warp + 1] : 0;
+  auto hist_y = [&](int r) { return __fdiv_rn(c.pval[r], c.Tabs); };
+
+  // 1. the row's largest scaled value
+  float ymax = -INFINITY;
+  bool bad = false;
+  for (int t = lane; t < nt; t += 32) ymax = fmaxf(ymax, tY[warp * c.tpw + t]);
+  for (int r = hr0 + lane; r < hr1; r += 32) {
+    const float y = hist_y(r);
+    bad |= (y != y) || y == INFINITY;
+    ymax = fmaxf(ymax, y);
+  }
+  if (__any_sync(kFull, bad) && lane == 0) atomicOr(&m->flags, F_NAN);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ymax = fmaxf(ymax, __shfl_xor_sync(kFull, ymax, o));
+  if (lane == 0) m->wbest[warp] = ymax;
+  __syncthreads();
+  const int st = status_from_flags(m->flags, false);
+  float M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) M = fmaxf(M, m->wbest[w]);
+  if (st != NS_OK || !(M > -INFINITY)) {
+    if (tid == 0) a.out_ids[row] = (st != NS_OK) ? st : NS_ERR_INVALID_DISTRIBUTION;
+    return;
+  }
+
+  // 2. this warp's mass
+  auto tile_scale = [&](int t) {
+    const float y = tY[warp * c.tpw + t];
+    return y > -INFINITY ? double(expf(__fsub_rn(y, M))) : 0.0;
+  };
+  double W = 0.0;
+  for (int t = lane; t < nt; t += 32) W += tD[warp * c.tpw + t] * tile_scale(t);
+  for (int r = hr0 + lane; r < hr1; r += 32) {
+    const float y = hist_y(r);
+    if (y > -INFINITY) W += double(expf(__fsub_rn(y, M)));
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) W += __shfl_xor_sync(kFull, W, o);
+  if (lane == 0) m->d_red[warp] = W;
+  __syncthreads();
+
+  // 3. the warp holding u * Z (the last warp with mass if rounding leaves the
+  // target past the end)
+  if (tid == 0) {
+    const float u = a.uniforms ? c.u_pre : philox_uniform(a.seed, a.offset, uint64_t(row));
+    double Z = 0.0;
+    for (int w = 0; w < kWarps; ++w) Z += m->d_red[w];
+    const double target = double(u) * Z;
+    double before = 0.0;
+    int sw = -1, last = 0;
+    for (int w = 0; w < kWarps; ++w) {
+      if (m->d_red[w] > 0.0) last = w;
+      if (sw < 0 && before + m->d_red[w] > target) sw = w;
+      if (sw < 0) before += m->d_red[w];
+    }
+    if (sw < 0) {
+      sw = last;
+      before = Z - m->d_red[last];
+    }
+    m->s_warp = sw;
+    m->s_rem = target - before;
+  }
+  __syncthreads();
+  if (warp != m->s_warp) return;
+
+  // 4. the tile: per-tile totals (scaled tile mass + its history columns),
+  // scanned in column order 32 tiles at a time
+  double rem = m->s_rem;
+  int ts = -1, tlast = 0;
+  for (int t0 = 0; t0 < nt && ts < 0; t0 += 32) {
+    const int t = t0 + lane;
+    double T = 0.0;
+    if (t < nt) {
+      T = tD[warp * c.tpw + t] * tile_scale(t);
+      if (c.pen) {
+        const int2 rr = tile_ranks(c, warp, t);
+        for (int r = rr.x; r < rr.y; ++r) {
+          const float y = hist_y(r);
+          if (y > -INFINITY) T += double(expf(__fsub_rn(y, M)));
+        }
+      }
+    }
+    double incl = T;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double v = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const unsigned hit = __ballot_sync(kFull, t < nt && incl > rem);
+    const unsigned nz = __ballot_sync(kFull, t < nt && T > 0.0);
+    if (nz) tlast = t0 + 31 - __clz(nz);
+    if (hit) {
+      const int l = __ffs(hit) - 1;
+      ts = t0 + l;
+      rem -= __shfl_sync(kFull, incl - T, l);
+    } else {
+      rem -= __shfl_sync(kFull, incl, 31);
+    }
+  }
+  if (ts < 0) {  // rounding left the target past the last tile: its last element
+    ts = tlast;
+    rem = INFINITY;
+  }
+
+  // 5. read tile ts again and scan it in column order, 32 consecutive
+  // elements per round (one per lane); history columns take their penalised
+  // values
+  const int sidx = 0;
+  const uint32_t parity = uint32_t((nt + 1) / 2) & 1u;  // phases stage 0 completed in the stream
+  if (lane == 0) issue_tile(c, warp, ts, sidx, policy);
+  if (!__all_sync(kFull, mbar_wait_bounded(c.sbar(warp, sidx), parity))) {
+    if (lane == 0) a.out_ids[row] = NS_ERR_DEVICE_TIMEOUT;
+    return;
+  }
+  __syncwarp();  // lane 0's plain-load head / tail
+  const R* sr = reinterpret_cast<const R*>(c.stage(warp, sidx));
+  const int len = c.tile_len(warp, ts), lead = c.tile_lead(warp, ts);
+  const int base = warp * c.pw + ts * TE;  // CTA-relative column of element 0
+  const float ym = tY[warp * c.tpw + ts];
+  const double f = tile_scale(ts);
+  int2 rr = make_int2(0, 0);
+  if (c.pen) rr = tile_ranks(c, warp, ts);
+  int pick = -1, lastnz = -1;
+  for (int e0 = 0; e0 < len; e0 += 32) {
+    const int e = e0 + lane;
+    double wgt = 0.0;
+    if (e < len) {
+      int hr = -1;
+      for (int r = rr.x; r < rr.y; ++r)
+        if (c.colr[r] - base == e) hr = r;
+      if (hr >= 0) {
+        const float y = hist_y(hr);
+        if (y > -INFINITY) wgt = double(expf(__fsub_rn(y, M)));
+      } else {
+        const float x = c.neg ? -E::widen(sr[lead + e]) : E::widen(sr[lead + e]);
+        if (ym > -INFINITY) wgt = double(softmax_weight(x, ym, c.Tabs, __frcp_rn(c.Tabs))) * f;
+      }
+    }
+    double incl = wgt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double v = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const unsigned nz = __ballot_sync(kFull, wgt > 0.0);
+    if (nz) lastnz = e0 + 31 - __clz(nz);
+    const unsigned hit = __ballot_sync(kFull, wgt > 0.0 && incl > rem);
+    if (hit) {
+      pick = e0 + __ffs(hit) - 1;
+      break;
+    }
+    rem -= __shfl_sync(kFull, incl, 31);
+  }
+  if (pick < 0) pick = lastnz;  // rounding left the target past the end: the last weighted element
+  if (lane == 0)
+    a.out_ids[row] = (pick >= 0) ? int64_t(c.c0 + base + pick) + a.vocab_offset : NS_ERR_INVALID_DISTRIBUTION;
 }
 
 // Leader, FAST rows: the K-th largest value over the union of every warp list
@@ -2260,6 +2553,9 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     mode = MODE_GREEDY;
   else if (topk > 0 && int64_t(topk) < a.vocab_total && topk <= kFastK)
     mode = MODE_FAST;
+  else if (!(topk > 0 && int64_t(topk) < a.vocab_total) && !(topp > 0.0f && topp < 1.0f) && CL == 1 &&
+           !a.vp_keys)
+    mode = MODE_SOFTMAX;
   else
     mode = MODE_GENERAL;
   if (a.vp_keys && mode == MODE_GENERAL) {  // no candidate record for these rows
@@ -2489,6 +2785,10 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     }
   }
   if (mode == MODE_FAST && s.ovf && lane == 0) atomicOr(&m->flags, F_OVF);
+  if (mode == MODE_SOFTMAX) {  // single-CTA rows only
+    softmax_tail(c, a, policy);
+    return;
+  }
   if (CL == 1 && mode != MODE_GENERAL && !a.vp_keys) {
     if (single_block_tail(c, a, mode, ok, s, best, bidx, topp)) return;
     __syncthreads();  // the row continues on the general merge below

@@ -186,6 +186,32 @@ def test_tie_plateau_merge_paths(sampler, n_ties, K, B):
     check(ids, ref, f"ties {n_ties} B={B}")
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_softmax_rows_top_k_and_top_p_off(sampler, dtype):
+    """The reference's default request (top_k -1, top_p 1.0): the draw is over
+    the whole softmax.  96 full-size rows run one block per row (the one-pass
+    softmax path); k 0 or >= V and p 0.0 also disable the filters."""
+    B, V = 96, 151936
+    x = make_logits(61, B, V, 3.0, spike_frac=0.005, dtype=dtype)
+    hs = make_histories(62, B, V, 256)
+    rng = np.random.default_rng(63)
+    params = []
+    for b in range(B):
+        pen = dict(repetition_penalty=1.2, presence_penalty=0.5, frequency_penalty=0.3) if b % 2 else {}
+        params.append(SamplingParams(temperature=float(rng.choice([0.7, 1.3, -0.8, 0.05])),
+                                     top_k=int(rng.choice([-1, 0, V, V + 5])),
+                                     top_p=float(rng.choice([1.0, 0.0])), **pen))
+    x[3, 1000] = float("nan")                  # an error row
+    xf = x.float()
+    xf[5, 77] = 3.0e38                         # x / T overflows for T < 1
+    params[5] = SamplingParams(temperature=0.7, top_k=-1, top_p=1.0)
+    u = make_uniforms(64, B)
+    x_in = xf.to(dtype) if dtype == torch.float32 else x
+    ids, ref = run(sampler, x_in, hs, params, u)
+    assert check(ids, ref, f"softmax {dtype}") <= 3
+    assert ids[3] < 0 and (dtype != torch.float32 or ids[5] < 0)
+
+
 def test_philox_default_stream_matches_oracle(sampler):
     from b200_sampler import B200Sampler
     s = B200Sampler(seed=99)
