@@ -119,7 +119,7 @@ int ns_vp_record_int64s(int64_t batch, int cap, int64_t* out_count);
  * vocab_local) of a vocab_total-wide row.  History ids are global ids; each
  * slice penalises the ones it holds.  Writes per row the top-k survivors
  * (ties at the k-th value kept) as keys, or for greedy rows (T == 0) one key.
- * Rows with top-k off or k > 128 report NS_ERR_UNSUPPORTED; more than `cap`
+ * Rows with top-k off or k > 240 report NS_ERR_UNSUPPORTED; more than `cap`
  * survivors report NS_ERR_CANDIDATE_OVERFLOW.  cap in [1, 1024].
  */
 int ns_vp_local(const void* logits, int dtype, int64_t batch, int64_t vocab_local, int64_t row_stride,

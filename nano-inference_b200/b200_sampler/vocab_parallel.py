@@ -31,7 +31,7 @@ from . import _lib
 from .params import pack_params
 from .sampler import _DTYPES, _ROW_ERRORS, B200Sampler
 
-FAST_MAX_K = 128       # largest top_k the candidate records serve (kFastK in the kernel)
+FAST_MAX_K = 240       # largest top_k the candidate records serve (kFastK in the kernel)
 MAX_CAP = 1024         # record capacity limit (kRankMax in the kernel)
 
 

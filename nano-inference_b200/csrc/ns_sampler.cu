@@ -63,7 +63,9 @@ constexpr int kWStageStride = kWTile + 32;      // + alignment lead + vector ove
 constexpr int kStageBytes = kWarps * kWStages * kWStageStride;
 constexpr int kCapW = 256;                      // per-warp candidate buffer (entries)
 constexpr int kPerLane = kCapW / 32;
-constexpr int kFastK = 128;                     // largest top_k served by the single-pass path
+constexpr int kFastK = 240;                     // largest top_k served by the single-pass path
+constexpr int kNucleusK = 128;                  // NUCLEUS candidates (the largest values with ties)
+static_assert((kFastK + kWarps - 1) / kWarps <= 32, "a warp's published rank is one of its 32 lane maxima");
 constexpr int kCandBytes = kWarps * kCapW * 8;  // candidate buffers (x, col)
 constexpr int kBins = 256;                      // radix digit = 8 bits (one bin per thread)
 static_assert(kBins == kThreads, "block_kth_regs clears one bin per thread");
@@ -74,7 +76,7 @@ static_assert(kMergeCap * 16 <= kStageBytes, "merge lists and their sort keys fi
 constexpr int kMaxLists = kMaxCluster * kWarps;
 constexpr unsigned kFull = 0xFFFFFFFFu;
 
-enum : int { MODE_GREEDY = 0, MODE_FAST = 1, MODE_GENERAL = 2, MODE_SOFTMAX = 3 };
+enum : int { MODE_GREEDY = 0, MODE_FAST = 1, MODE_GENERAL = 2, MODE_SOFTMAX = 3, MODE_NUCLEUS = 4 };
 enum : int { F_NAN = 1, F_BADID = 2, F_HIST = 4, F_OVF = 8, F_TIMEOUT = 16, F_UNSUP = 32 };
 
 // ---------------------------------------------------------------------------
@@ -1071,6 +1073,12 @@ __device__ __forceinline__ bool stream_warp(const Ctx<DT>& c, int mode, uint64_t
         fast_tile<DT, true>(c, s, w, t, st, t < nfull);
       else
         fast_tile<DT, false>(c, s, w, t, st, t < nfull);
+      if (mode == MODE_NUCLEUS) {
+        if (c.neg)
+          mass_tile<DT, true>(c, w, t, st, t < nfull);
+        else
+          mass_tile<DT, false>(c, w, t, st, t < nfull);
+      }
       if (t == 1 || t == 4 || t == 9) publish_bound(c, s);
       read_shared_tau(c, s);
     }
@@ -1226,7 +1234,8 @@ __device__ __forceinline__ int status_from_flags(int f, bool greedy) {
 constexpr int kSmallN = 128;
 
 template <int DT>
-__device__ void finalize_small_sorted(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, int n);
+__device__ void finalize_small_sorted(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, int n,
+                                      double norm = -1.0);
 
 // Leader, FAST rows with n <= kSmallN survivors: sort by rank counting (thread
 // i owns survivor i), then one warp computes the softmax prefix sums with
@@ -1256,8 +1265,11 @@ __device__ void finalize_small(const Ctx<DT>& c, const KArgs& a, int64_t row, fl
 // Leader, FAST rows: n <= kSmallN survivors already in (y desc, id asc) order
 // in sy[] / sid[]; one warp computes the softmax prefix sums with shuffles (4
 // positions per lane).
+// norm > 0: the softmax's normaliser is the row's total mass (top-k off), not
+// the survivors' sum.
 template <int DT>
-__device__ void finalize_small_sorted(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, int n) {
+__device__ void finalize_small_sorted(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, int n,
+                                      double norm) {
   Misc* m = c.m;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float* sy = reinterpret_cast<float*>(c.stages + size_t(a.merge_cap) * 8);
@@ -1297,7 +1309,7 @@ __device__ void finalize_small_sorted(const Ctx<DT>& c, const KArgs& a, int64_t 
       for (int k = 0; k < 4; ++k) {
         const int j = lane * 4 + k;
         run += e[k];
-        cnt += (j <= n - 2 && run <= double(topp) * total) ? 1 : 0;
+        cnt += (j <= n - 2 && run <= double(topp) * (norm > 0.0 ? norm : total)) ? 1 : 0;
       }
       L = 1 + int(__reduce_add_sync(kFull, unsigned(cnt)));
     }
@@ -1514,7 +1526,7 @@ __device__ __forceinline__ void gather_keys(const Ctx<DT>& c, cg::cluster_group&
 
 template <int DT>
 __device__ void finalize_keys(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, const uint64_t* sorted,
-                              int n, int n_all);
+                              int n, int n_all, double norm = -1.0);
 
 template <int DT>
 __device__ void rank_finalize(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, int n) {
@@ -1547,7 +1559,7 @@ __device__ void rank_finalize(const Ctx<DT>& c, const KArgs& a, int64_t row, flo
 // run itself.  A tie run that reaches past the n placed keys overflows.
 template <int DT>
 __device__ void finalize_keys(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, const uint64_t* sorted,
-                              int n, int n_all) {
+                              int n, int n_all, double norm) {
   Misc* m = c.m;
   const int tid = threadIdx.x, lane = tid & 31;
   if (n == 0) {  // nothing finite (a vocab-parallel slice may legitimately hold none)
@@ -1590,7 +1602,7 @@ __device__ void finalize_keys(const Ctx<DT>& c, const KArgs& a, int64_t row, flo
       sid[tid] = int(~uint32_t(sorted[tid]));
     }
     __syncthreads();
-    finalize_small_sorted(c, a, row, topp, nfin);
+    finalize_small_sorted(c, a, row, topp, nfin, norm);
     return;
   }
   float* my = reinterpret_cast<float*>(c.stages);
@@ -1649,10 +1661,22 @@ __device__ bool single_block_tail(const Ctx<DT>& c, const KArgs& a, int mode, bo
     return true;
   }
   // every warp's final bound, then only survivors of the tightest become keys
+  const bool nuc = (mode == MODE_NUCLEUS);
+  if (nuc) {  // the row's largest scaled value, for its total mass
+    const float ym = warp_row_max(c);
+    if (lane == 0) m->wbest[warp] = ym;
+  }
   if (ok) publish_bound(c, s);
   __syncthreads();
   WarpCand f = s;
   read_shared_tau(c, f);
+  float M = -INFINITY;
+  if (nuc) {
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, m->wbest[w]);
+    const double W = (M > -INFINITY) ? warp_row_mass(c, M) : 0.0;
+    if (lane == 0) m->d_red[warp] = W;
+  }
   uint64_t* keys = reinterpret_cast<uint64_t*>(c.stage(warp, 0));
   int nw = 0;
   if (ok && !s.ovf) {
@@ -1682,7 +1706,16 @@ __device__ bool single_block_tail(const Ctx<DT>& c, const KArgs& a, int mode, bo
   int n = 0;
 #pragma unroll
   for (int w = 0; w < kWarps; ++w) n += m->wn[w];
-  if (n > kRankMax) return false;  // a union this large takes the radix-select merge
+  if (n > kRankMax) {  // a union this large takes the radix-select merge (NUCLEUS: the multi-pass path)
+    if (nuc && tid == 0) atomicOr(&m->flags, F_OVF);
+    return false;
+  }
+  double Z = -1.0;
+  if (nuc) {
+    Z = 0.0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) Z += m->d_red[w];
+  }
   uint64_t* sorted = reinterpret_cast<uint64_t*>(c.cx);
   for (int i = lane; i < nw; i += 32) {
     const uint64_t ki = keys[i];
@@ -1699,8 +1732,76 @@ __device__ bool single_block_tail(const Ctx<DT>& c, const KArgs& a, int mode, bo
     if (pos < kRankMax) sorted[pos] = ki;
   }
   __syncthreads();
-  finalize_keys(c, a, row, topp, sorted, n, n);
+  if (nuc) {
+    // the kNucleusK largest with ties must hold more than p of the row's mass
+    // (with a margin above the sums' rounding), else the multi-pass path
+    if (warp == 0) {
+      const int kk = min(c.K, n);
+      const uint32_t yk = uint32_t(sorted[kk - 1] >> 32);
+      int nfin = n;
+      for (int j0 = kk; j0 < n; j0 += 32) {
+        const unsigned b = __ballot_sync(kFull, j0 + lane < n && uint32_t(sorted[j0 + lane] >> 32) < yk);
+        if (b) {
+          nfin = j0 + __ffs(b) - 1;
+          break;
+        }
+      }
+      double cm = 0.0;
+      for (int j = lane; j < nfin; j += 32) cm += double(expf(__fsub_rn(key2f(uint32_t(sorted[j] >> 32)), M)));
+#pragma unroll
+      for (int o = 16; o; o >>= 1) cm += __shfl_xor_sync(kFull, cm, o);
+      const bool covered = nfin <= kSmallN && M > -INFINITY && cm > (double(topp) + 1e-6) * Z;
+      if (lane == 0 && !covered) atomicOr(&m->flags, F_OVF);
+    }
+    __syncthreads();
+    if (m->flags & F_OVF) return false;
+  }
+  finalize_keys(c, a, row, topp, sorted, n, n, Z);
   return true;
+}
+
+// SOFTMAX / NUCLEUS, after the stream (tile masses in place, penalised
+// history values computed): this warp's largest scaled value over its tiles
+// and its history columns (NaN or +inf there flags F_NAN), warp-uniform ...
+template <int DT>
+__device__ __forceinline__ float warp_row_max(const Ctx<DT>& c) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float* tY = softmax_tile_max(c);
+  float ymax = -INFINITY;
+  bool bad = false;
+  for (int t = lane; t < c.wtiles(warp); t += 32) ymax = fmaxf(ymax, tY[warp * c.tpw + t]);
+  if (c.pen)
+    for (int r = c.m->segoff[warp] + lane; r < c.m->segoff[warp + 1]; r += 32) {
+      const float y = __fdiv_rn(c.pval[r], c.Tabs);
+      bad |= (y != y) || y == INFINITY;
+      ymax = fmaxf(ymax, y);
+    }
+  if (__any_sync(kFull, bad) && lane == 0) atomicOr(&c.m->flags, F_NAN);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ymax = fmaxf(ymax, __shfl_xor_sync(kFull, ymax, o));
+  return ymax;
+}
+
+// ... and this warp's mass with the row's largest scaled value M: tile masses
+// times expf(ym_t - M) plus expf(y - M) of its history columns (float64).
+template <int DT>
+__device__ __forceinline__ double warp_row_mass(const Ctx<DT>& c, float M) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const double* tD = softmax_tile_mass(c.tacc);
+  const float* tY = softmax_tile_max(c);
+  double W = 0.0;
+  for (int t = lane; t < c.wtiles(warp); t += 32) {
+    const float y = tY[warp * c.tpw + t];
+    if (y > -INFINITY) W += tD[warp * c.tpw + t] * double(expf(__fsub_rn(y, M)));
+  }
+  if (c.pen)
+    for (int r = c.m->segoff[warp] + lane; r < c.m->segoff[warp + 1]; r += 32) {
+      const float y = __fdiv_rn(c.pval[r], c.Tabs);
+      if (y > -INFINITY) W += double(expf(__fsub_rn(y, M)));
+    }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) W += __shfl_xor_sync(kFull, W, o);
+  return W;
 }
 
 // SOFTMAX rows on one CTA: after the stream (tile masses in place, penalised
@@ -1720,21 +1821,10 @@ __device__ void softmax_tail(const Ctx<DT>& c, const KArgs& a, uint64_t policy) 
   const double* tD = softmax_tile_mass(c.tacc);
   const float* tY = softmax_tile_max(c);
   const int nt = c.wtiles(warp);
-  const int hr0 = c.pen ? m->segoff[warp] : 0, hr1 = c.pen ? m->segoff[warp + 1] : 0;
   auto hist_y = [&](int r) { return __fdiv_rn(c.pval[r], c.Tabs); };
 
   // 1. the row's largest scaled value
-  float ymax = -INFINITY;
-  bool bad = false;
-  for (int t = lane; t < nt; t += 32) ymax = fmaxf(ymax, tY[warp * c.tpw + t]);
-  for (int r = hr0 + lane; r < hr1; r += 32) {
-    const float y = hist_y(r);
-    bad |= (y != y) || y == INFINITY;
-    ymax = fmaxf(ymax, y);
-  }
-  if (__any_sync(kFull, bad) && lane == 0) atomicOr(&m->flags, F_NAN);
-#pragma unroll
-  for (int o = 16; o; o >>= 1) ymax = fmaxf(ymax, __shfl_xor_sync(kFull, ymax, o));
+  const float ymax = warp_row_max(c);
   if (lane == 0) m->wbest[warp] = ymax;
   __syncthreads();
   const int st = status_from_flags(m->flags, false);
@@ -1745,20 +1835,13 @@ __device__ void softmax_tail(const Ctx<DT>& c, const KArgs& a, uint64_t policy) 
     if (tid == 0) a.out_ids[row] = (st != NS_OK) ? st : NS_ERR_INVALID_DISTRIBUTION;
     return;
   }
-
-  // 2. this warp's mass
   auto tile_scale = [&](int t) {
     const float y = tY[warp * c.tpw + t];
     return y > -INFINITY ? double(expf(__fsub_rn(y, M))) : 0.0;
   };
-  double W = 0.0;
-  for (int t = lane; t < nt; t += 32) W += tD[warp * c.tpw + t] * tile_scale(t);
-  for (int r = hr0 + lane; r < hr1; r += 32) {
-    const float y = hist_y(r);
-    if (y > -INFINITY) W += double(expf(__fsub_rn(y, M)));
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) W += __shfl_xor_sync(kFull, W, o);
+
+  // 2. this warp's mass
+  const double W = warp_row_mass(c, M);
   if (lane == 0) m->d_red[warp] = W;
   __syncthreads();
 
@@ -2553,18 +2636,21 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     mode = MODE_GREEDY;
   else if (topk > 0 && int64_t(topk) < a.vocab_total && topk <= kFastK)
     mode = MODE_FAST;
-  else if (!(topk > 0 && int64_t(topk) < a.vocab_total) && !(topp > 0.0f && topp < 1.0f) && CL == 1 &&
-           !a.vp_keys)
-    mode = MODE_SOFTMAX;
+  else if (!(topk > 0 && int64_t(topk) < a.vocab_total) && CL == 1 && !a.vp_keys)
+    mode = (topp > 0.0f && topp < 1.0f) ? MODE_NUCLEUS : MODE_SOFTMAX;
   else
     mode = MODE_GENERAL;
+  // NUCLEUS (top-k off, top-p on): the FAST filter keeps the kNucleusK largest
+  // with ties as candidates, and the tile masses give the row's total; when the
+  // candidates hold more than p of it the cut lies among them
+  const bool fastlike = (mode == MODE_FAST || mode == MODE_NUCLEUS);
   if (a.vp_keys && mode == MODE_GENERAL) {  // no candidate record for these rows
     if (rank == 0 && tid == 0) a.out_ids[row] = NS_ERR_UNSUPPORTED;
     return;
   }
   c.neg = T < 0.0f;
   c.Tabs = fabsf(T);
-  c.K = topk;
+  c.K = (mode == MODE_NUCLEUS) ? kNucleusK : topk;
   int64_t h0 = 0, h1 = 0;
   if (a.hist_offsets) {
     h0 = a.hist_offsets[row];
@@ -2738,7 +2824,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
   float best = -INFINITY;
   int bidx = INT_MAX;
   int n_ready = 0;
-  if (mode == MODE_FAST) {
+  if (fastlike) {
     // Seed: each warp publishes the kq-th largest of its 32 lane maxima over
     // its first kWStages tiles (distinct elements); after one block barrier
     // every warp starts from the shared bound.
@@ -2776,7 +2862,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
           bidx = col;
         }
       }
-    } else if (mode == MODE_FAST && !s.ovf) {
+    } else if (fastlike && !s.ovf) {
       for (int r0 = hr0; r0 < hr1; r0 += 32) {
         const int r = r0 + lane;
         const bool has = r < hr1;
@@ -2784,7 +2870,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
       }
     }
   }
-  if (mode == MODE_FAST && s.ovf && lane == 0) atomicOr(&m->flags, F_OVF);
+  if (fastlike && s.ovf && lane == 0) atomicOr(&m->flags, F_OVF);
   if (mode == MODE_SOFTMAX) {  // single-CTA rows only
     softmax_tail(c, a, policy);
     return;
@@ -2793,7 +2879,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     if (single_block_tail(c, a, mode, ok, s, best, bidx, topp)) return;
     __syncthreads();  // the row continues on the general merge below
   }
-  if (mode == MODE_FAST) {  // every warp's final bound; survivors of the tightest
+  if (fastlike) {  // every warp's final bound; survivors of the tightest
     if (ok) publish_bound(c, s);
     __syncthreads();
     if (!s.ovf) {
@@ -2813,7 +2899,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     }
   }
   if (lane == 0) {
-    m->wn[warp] = (mode == MODE_FAST && ok && !s.ovf) ? s.n : 0;
+    m->wn[warp] = (fastlike && ok && !s.ovf) ? s.n : 0;
     m->wbest[warp] = best;
     m->widx[warp] = bidx;
   }
@@ -2845,8 +2931,9 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
       if (rank == 0 && tid == 0) a.out_ids[row] = NS_ERR_CANDIDATE_OVERFLOW;
       return;
     }
-    if (mode == MODE_GENERAL || (mode == MODE_FAST && (fl_all & F_OVF) && !hard)) {
+    if (mode == MODE_GENERAL || (fastlike && (fl_all & F_OVF) && !hard)) {
       cluster.sync();
+      c.K = topk;  // NUCLEUS rows filtered with kNucleusK
       if (tid == 0) m->flags &= ~F_OVF;
       __syncthreads();
       int seq = (mode == MODE_GENERAL) ? 0 : c.wtiles(warp);

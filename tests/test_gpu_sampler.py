@@ -212,6 +212,31 @@ def test_softmax_rows_top_k_and_top_p_off(sampler, dtype):
     assert ids[3] < 0 and (dtype != torch.float32 or ids[5] < 0)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_nucleus_rows_top_k_off(sampler, dtype):
+    """Top-k off with top-p on: the one-pass path keeps the 128 largest as
+    candidates and checks they hold more than p of the row's mass; rows whose
+    nucleus is larger (a flat row, a wide plateau) take the multi-pass path."""
+    B, V = 96, 151936
+    x = make_logits(71, B, V, 3.0, spike_frac=0.005, dtype=torch.float32)
+    x[7] = torch.randn(V, generator=torch.Generator().manual_seed(7)) * 0.01    # nucleus ~ 0.9 V
+    x[9, :300] = 8.0 + torch.arange(300, dtype=torch.float32) * 1e-3            # ~300 near-equal leaders
+    x = x.to(dtype)
+    hs = make_histories(72, B, V, 256)
+    rng = np.random.default_rng(73)
+    params = []
+    for b in range(B):
+        pen = dict(repetition_penalty=1.1, presence_penalty=0.4, frequency_penalty=0.2) if b % 3 == 0 else {}
+        params.append(SamplingParams(temperature=float(rng.choice([0.7, 1.0, -0.9, 1.5])),
+                                     top_k=int(rng.choice([-1, 0, V])),
+                                     top_p=float(rng.choice([0.5, 0.9, 0.95, 0.99])), **pen))
+    params[7] = SamplingParams(temperature=1.0, top_k=-1, top_p=0.9)
+    params[9] = SamplingParams(temperature=1.0, top_k=-1, top_p=0.9)
+    u = make_uniforms(74, B)
+    ids, ref = run(sampler, x, hs, params, u)
+    assert check(ids, ref, f"nucleus {dtype}") <= 3
+
+
 def test_philox_default_stream_matches_oracle(sampler):
     from b200_sampler import B200Sampler
     s = B200Sampler(seed=99)
