@@ -1,40 +1,49 @@
 // B200-native token sampler (sm_100a).
 //
-// One launch samples every row of a batch.  Each row is handled by a thread
-// block cluster of C CTAs (C chosen so rows x C covers the SMs); CTA r owns
-// columns [r*per_cta, (r+1)*per_cta) of the row, and each of its 8 warps owns
-// a contiguous 1/8 of that range.  A warp streams its columns once from HBM
-// through its own 2-stage ring of 4 KB bulk copies (TMA, cp.async.bulk) into
-// shared memory and consumes them with no block-wide barrier: its threshold,
-// candidate buffer and argmax live in warp-uniform registers and warp-private
-// shared memory.  Block and cluster synchronisation happens only at the
-// merge, where the cluster leader combines all warps of all CTAs through
-// distributed shared memory.  Per row, by mode:
+// One launch samples every row of a batch.  Each row is handled by one CTA
+// (256 threads), or by a thread block cluster of up to 8 CTAs when the batch
+// is too small to fill the SMs; CTA r owns columns [r*per_cta, (r+1)*per_cta)
+// of the row, and each of its 8 warps owns a contiguous 1/8 of that range.  A
+// warp streams its columns once from HBM through its own 2-stage ring of 4 KB
+// bulk copies (TMA, cp.async.bulk) into shared memory and consumes them with
+// no block-wide barrier: its threshold, candidate buffer and argmax live in
+// warp-uniform registers and warp-private shared memory.  Block (and cluster)
+// synchronisation happens at the seed and at the end of the row.  Per row, by
+// mode:
 //
 //   GREEDY (temperature == 0; reference sampler.py:60-70)
 //       first-index argmax of the penalised logits (NaN counts as max).
 //   FAST   (0 < top_k <= kFastK; reference sampler.py:73-89, 110-133)
-//       single-pass threshold filter: each warp keeps every logit >= a
-//       running lower bound tau of its local k-th largest value; when its
-//       256-entry buffer fills, a warp-level bitwise radix select raises tau
-//       and compacts (the vocabulary is never sorted).  The leader selects
-//       the global k-th value over the union, then runs top-p and the
-//       inverse-CDF draw on the survivors.
-//   GENERAL (top-k disabled or larger than kFastK): reported as
-//       NS_ERR_UNSUPPORTED by this version.
+//       single-pass threshold filter: each warp keeps every value >= tau, a
+//       lower bound of the CTA's k-th largest shared between the warps without
+//       barriers; the survivors of the tightest bound are sorted as 64-bit keys
+//       (scaled value, id), and the top-k with ties, top-p and the inverse-CDF
+//       draw run on them.  The vocabulary is never sorted.
+//   SOFTMAX (top-k and top-p both off -- the reference's defaults)
+//       one pass of per-tile maxima and float64 masses; the draw is located by
+//       warp, then tile, and one 4 KB tile is read again.
+//   NUCLEUS (top-k off, top-p on)
+//       FAST with the kNucleusK largest as candidates plus the SOFTMAX masses;
+//       when the candidates hold more than p of the row's mass, the top-p cut
+//       and the draw run on them; otherwise the row continues on GENERAL.
+//   GENERAL (top-k > kFastK, ties overflowing a buffer, NUCLEUS rows whose
+//       nucleus is larger, and rows of clusters with top-k off)
+//       a cluster-cooperative multi-pass radix search over counts and
+//       fixed-point masses; the last pass rescans one tile in id order.
 //
 // Penalties (reference sampler.py:93-108 plus presence/frequency): before the
-// stream starts, each CTA hashes the row's history ids that fall in its
-// columns (id -> count) and buckets the distinct ids by warp tile.  When a
-// tile lands, its bucket's logits are penalised in fp32 (IEEE division /
-// multiplication / subtraction, never contracted into FMAs), kept aside, and
-// their slots overwritten with -inf so the streaming filter sees only
-// un-penalised columns.
+// stream starts, each CTA sets a column bitmap from the row's history ids,
+// ranks the distinct ids in column order and counts their occurrences (shared
+// atomics without return values).  When a tile lands, its history slots --
+// one rank range -- have their raw values recorded and are overwritten with
+// -inf so the streaming passes see only un-penalised columns; after its last
+// tile each warp penalises its recorded values in fp32 (IEEE division /
+// multiplication / subtraction, never contracted into FMAs) and adds them once.
 //
-// Temperature is applied without a per-element division: y = x / T is
-// monotone in x, so the k-th largest y is rn(x_k / T) and the survivors
-// {rn(x / T) >= rn(x_k / T)} are exactly {x >= x_lo} for the smallest x_lo
-// with rn(x_lo / T) >= rn(x_k / T), found by a short search over float keys.
+// Temperature is applied without a per-element division on the FAST path: y
+// = x / T is monotone in x, so the survivors {rn(x / T) >= rn(x_k / T)} are
+// {x >= x_lo} for the smallest x_lo with rn(x_lo / T) >= rn(x_k / T) (found by
+// a short search over float keys, or bounded from below without divisions).
 // Negative temperatures are handled by negating x (rn(-x / -T) = rn(x / T)).
 #include <cooperative_groups.h>
 #include <cuda_bf16.h>
