@@ -86,7 +86,7 @@ constexpr int kMaxLists = kMaxCluster * kWarps;
 constexpr unsigned kFull = 0xFFFFFFFFu;
 
 enum : int { MODE_GREEDY = 0, MODE_FAST = 1, MODE_GENERAL = 2, MODE_SOFTMAX = 3, MODE_NUCLEUS = 4 };
-enum : int { F_NAN = 1, F_BADID = 2, F_HIST = 4, F_OVF = 8, F_TIMEOUT = 16, F_UNSUP = 32 };
+enum : int { F_NAN = 1, F_BADID = 2, F_HIST = 4, F_OVF = 8, F_TIMEOUT = 16, F_UNSUP = 32, F_BIG = 64 };
 
 // ---------------------------------------------------------------------------
 // element types
@@ -1512,6 +1512,8 @@ constexpr size_t kRankKeysOff = size_t(kMergeCap) * 8 + size_t(kRankMax) * 8;
 static_assert(size_t(kMergeCap) * 8 + 5 * kSmallN * 4 <= size_t(kMergeCap) * 8 + size_t(kRankMax) * 8,
               "finalize_small's arrays fit below the rank keys");
 static_assert(kRankKeysOff + 2 * size_t(kRankMax) * 8 <= size_t(kStageBytes), "rank-sort keys fit the stage area");
+constexpr int kMergeStage = kMergeCap;  // union keys the merge stages (32 KB at the stage area's start)
+static_assert(size_t(kMergeStage) * 8 <= kRankKeysOff, "staged lists end before the sorted keys");
 
 template <int DT>
 __device__ __forceinline__ void gather_keys(const Ctx<DT>& c, cg::cluster_group& cluster, int CL) {
@@ -1625,19 +1627,83 @@ __device__ void finalize_keys(const Ctx<DT>& c, const KArgs& a, int64_t row, flo
   finalize_row(c, a, row, topp);
 }
 
-// Rows on one CTA (cluster size 1), GREEDY and FAST: the end of the row with
-// few block barriers.  FAST: after every warp published its final bound, each
-// warp turns its survivors of the tightest bound into keys
-// (f2key(x / T) << 32) | ~id in its own stage bytes (its copies are all
-// consumed); after one barrier each warp places its keys in the union by
-// counting the keys above them in all eight lists, into the candidate buffers
-// (no longer read), and finalize_keys takes the top-k with ties.  Returns
-// false (the same on every thread) when the row continues on the general
-// merge below: tied values that overflowed a buffer (multi-pass path) or a
-// union of more than kRankMax survivors (radix-select merge).
+// Merge nl descending lists of distinct keys (list l at lists[roff[l] ..
+// roff[l + 1])) into sorted[0 .. min(n, kRankMax)): a key's position is its
+// index in its own list plus, for every other list, the keys above it (binary
+// search).  All threads of the block call it; a barrier follows.
+__device__ __forceinline__ void place_sorted_lists(const uint64_t* lists, const int* roff, int nl, int n,
+                                                   uint64_t* sorted) {
+  for (int e = threadIdx.x; e < n; e += kThreads) {
+    int r = 0;
+    while (roff[r + 1] <= e) ++r;
+    const uint64_t key = lists[e];
+    int pos = e - roff[r];
+    for (int r2 = 0; r2 < nl; ++r2) {
+      if (r2 == r) continue;
+      const uint64_t* l2 = lists + roff[r2];
+      int lo = 0, hi = roff[r2 + 1] - roff[r2];
+      while (lo < hi) {  // keys of list r2 above `key`
+        const int mid = (lo + hi) >> 1;
+        if (l2[mid] > key)
+          lo = mid + 1;
+        else
+          hi = mid;
+      }
+      pos += lo;
+    }
+    if (pos < kRankMax) sorted[pos] = key;
+  }
+  __syncthreads();
+}
+
+// Number of keys kept by top-k with ties: the first k of the descending keys
+// and every later key whose scaled value ties the k-th (reference
+// sampler.py:116-121).  Every warp may call it; it is warp-uniform.
+__device__ __forceinline__ int topk_with_ties(const uint64_t* sorted, int n, int K) {
+  const int lane = threadIdx.x & 31;
+  if (n == 0) return 0;
+  const int kk = min(K, n);
+  const uint32_t yk = uint32_t(sorted[kk - 1] >> 32);
+  for (int j0 = kk; j0 < n; j0 += 32) {
+    const unsigned b = __ballot_sync(kFull, j0 + lane < n && uint32_t(sorted[j0 + lane] >> 32) < yk);
+    if (b) return j0 + __ffs(b) - 1;
+  }
+  return n;
+}
+
+// A greedy row's result: the id, or (vocab-parallel local step) a one-key
+// record in which NaN sorts above every value.
+__device__ __forceinline__ void write_greedy(const KArgs& a, int64_t row, int st, float b, int bi) {
+  if (st != NS_OK) {
+    a.out_ids[row] = int64_t(st);
+  } else if (a.vp_keys) {
+    const uint32_t hi = (b != b) ? 0xFFFFFFFFu : f2key(b + 0.0f);
+    const uint32_t gid = uint32_t(int64_t(bi) + a.vocab_offset);
+    a.vp_keys[row * a.vp_cap] = int64_t((uint64_t(hi) << 32) | uint64_t(~gid));
+    a.out_ids[row] = 1;
+  } else {
+    a.out_ids[row] = int64_t(bi) + a.vocab_offset;
+  }
+}
+
+// The end of a GREEDY, FAST or NUCLEUS row (NUCLEUS: one CTA only) with few
+// barriers.
+// GREEDY: each CTA reduces its warps' (value, first index); a cluster's
+// leader reads the CTAs' results in parallel.
+// FAST / NUCLEUS: after every warp published its final bound, each warp turns
+// its survivors of the tightest bound into keys (f2key(x / T) << 32) | ~id in
+// its own stage bytes (its copies are all consumed); each warp places its keys
+// in the CTA's union by counting the keys above them in all eight lists, into
+// the candidate buffers (no longer read).  One CTA: finalize_keys takes the
+// top-k with ties.  A cluster: each CTA keeps its own top-k with ties (which
+// holds every element of the row's top-k that it owns), and the leader merges
+// the CTAs' lists through distributed shared memory.
+// Returns false (the same on every thread of the cluster) when the row
+// continues on the general merge below: tied values that overflowed a buffer
+// (multi-pass path), or a union of more than kRankMax survivors.
 template <int DT>
-__device__ bool single_block_tail(const Ctx<DT>& c, const KArgs& a, int mode, bool ok, const WarpCand& s, float best,
-                                  int bidx, float topp) {
+__device__ bool row_tail(const Ctx<DT>& c, const KArgs& a, cg::cluster_group& cluster, int CL, int rank, int mode,
+                         bool ok, const WarpCand& s, float best, int bidx, float topp) {
   Misc* m = c.m;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t row = c.row;
@@ -1664,9 +1730,34 @@ __device__ bool single_block_tail(const Ctx<DT>& c, const KArgs& a, int mode, bo
           b = m->wbest[w];
           bi = m->widx[w];
         }
-      const int st = status_from_flags(m->flags, true);
-      a.out_ids[row] = (st != NS_OK) ? int64_t(st) : int64_t(bi) + a.vocab_offset;
+      m->g_best = b;
+      m->g_idx = bi;
+      if (CL == 1) write_greedy(a, row, status_from_flags(m->flags, true), b, bi);
     }
+    if (CL == 1) return true;
+    cluster.sync();
+    if (rank == 0 && warp == 0) {
+      float b = -INFINITY;
+      int bi = INT_MAX, fl = 0;
+      if (lane < CL) {
+        const Misc* rm = cluster.map_shared_rank(m, lane);
+        b = rm->g_best;
+        bi = rm->g_idx;
+        fl = rm->flags;
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        const float ob = __shfl_xor_sync(kFull, b, o);
+        const int oi = __shfl_xor_sync(kFull, bi, o);
+        fl |= __shfl_xor_sync(kFull, fl, o);
+        if (better(ob, oi, b, bi)) {
+          b = ob;
+          bi = oi;
+        }
+      }
+      if (lane == 0) write_greedy(a, row, status_from_flags(fl, true), b, bi);
+    }
+    cluster.sync();  // the leader's reads are done before any CTA exits
     return true;
   }
   // every warp's final bound, then only survivors of the tightest become keys
@@ -1705,67 +1796,107 @@ __device__ bool single_block_tail(const Ctx<DT>& c, const KArgs& a, int mode, bo
     m->wn[warp] = nw;
   }
   __syncthreads();
-  const int fl = m->flags;
-  if ((fl & F_OVF) && !(fl & (F_NAN | F_TIMEOUT | F_BADID | F_HIST))) return false;
-  const int st = status_from_flags(fl, false);
-  if (st != NS_OK) {
-    if (tid == 0) a.out_ids[row] = st;
-    return true;
-  }
   int n = 0;
 #pragma unroll
   for (int w = 0; w < kWarps; ++w) n += m->wn[w];
-  if (n > kRankMax) {  // a union this large takes the radix-select merge (NUCLEUS: the multi-pass path)
-    if (nuc && tid == 0) atomicOr(&m->flags, F_OVF);
-    return false;
-  }
-  double Z = -1.0;
-  if (nuc) {
-    Z = 0.0;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) Z += m->d_red[w];
-  }
+  // A union past kRankMax: one CTA keeps its candidate buffers (no local sort)
+  // for the radix-select merge; NUCLEUS rows and clusters (whose other CTAs
+  // reuse their buffers for the sort) take the multi-pass path.
+  if (n > kRankMax && tid == 0) atomicOr(&m->flags, (nuc || CL > 1) ? F_OVF : F_BIG);
   uint64_t* sorted = reinterpret_cast<uint64_t*>(c.cx);
-  for (int i = lane; i < nw; i += 32) {
-    const uint64_t ki = keys[i];
-    int pos = 0;
-    for (int w2 = 0; w2 < kWarps; ++w2) {
-      const uint64_t* k2 = reinterpret_cast<const uint64_t*>(c.stage(w2, 0));
-      const int n2 = m->wn[w2];
+  if (n <= kRankMax) {
+    for (int i = lane; i < nw; i += 32) {
+      const uint64_t ki = keys[i];
+      int pos = 0;
+      for (int w2 = 0; w2 < kWarps; ++w2) {
+        const uint64_t* k2 = reinterpret_cast<const uint64_t*>(c.stage(w2, 0));
+        const int n2 = m->wn[w2];
 #pragma unroll 4
-      for (int j = 0; j < n2; j += 2) {
-        const ulonglong2 p = *reinterpret_cast<const ulonglong2*>(k2 + j);
-        pos += ((p.x > ki) ? 1 : 0) + ((p.y > ki) ? 1 : 0);
-      }
-    }
-    if (pos < kRankMax) sorted[pos] = ki;
-  }
-  __syncthreads();
-  if (nuc) {
-    // the kNucleusK largest with ties must hold more than p of the row's mass
-    // (with a margin above the sums' rounding), else the multi-pass path
-    if (warp == 0) {
-      const int kk = min(c.K, n);
-      const uint32_t yk = uint32_t(sorted[kk - 1] >> 32);
-      int nfin = n;
-      for (int j0 = kk; j0 < n; j0 += 32) {
-        const unsigned b = __ballot_sync(kFull, j0 + lane < n && uint32_t(sorted[j0 + lane] >> 32) < yk);
-        if (b) {
-          nfin = j0 + __ffs(b) - 1;
-          break;
+        for (int j = 0; j < n2; j += 2) {
+          const ulonglong2 p = *reinterpret_cast<const ulonglong2*>(k2 + j);
+          pos += ((p.x > ki) ? 1 : 0) + ((p.y > ki) ? 1 : 0);
         }
       }
-      double cm = 0.0;
-      for (int j = lane; j < nfin; j += 32) cm += double(expf(__fsub_rn(key2f(uint32_t(sorted[j] >> 32)), M)));
+      sorted[pos] = ki;
+    }
+  }
+  __syncthreads();
+  if (CL == 1) {
+    const int fl1 = m->flags;
+    if ((fl1 & (F_OVF | F_BIG)) && !(fl1 & (F_NAN | F_TIMEOUT | F_BADID | F_HIST))) return false;
+    const int st = status_from_flags(fl1, false);
+    if (st != NS_OK) {
+      if (tid == 0) a.out_ids[row] = st;
+      return true;
+    }
+    double Z = -1.0;
+    if (nuc) {
+      // the kNucleusK largest with ties must hold more than p of the row's
+      // mass (with a margin above the sums' rounding), else the multi-pass path
+      Z = 0.0;
 #pragma unroll
-      for (int o = 16; o; o >>= 1) cm += __shfl_xor_sync(kFull, cm, o);
-      const bool covered = nfin <= kSmallN && M > -INFINITY && cm > (double(topp) + 1e-6) * Z;
-      if (lane == 0 && !covered) atomicOr(&m->flags, F_OVF);
+      for (int w = 0; w < kWarps; ++w) Z += m->d_red[w];
+      if (warp == 0) {
+        const int nfin = topk_with_ties(sorted, n, c.K);
+        double cm = 0.0;
+        for (int j = lane; j < nfin; j += 32) cm += double(expf(__fsub_rn(key2f(uint32_t(sorted[j] >> 32)), M)));
+#pragma unroll
+        for (int o = 16; o; o >>= 1) cm += __shfl_xor_sync(kFull, cm, o);
+        const bool covered = nfin > 0 && nfin <= kSmallN && M > -INFINITY && cm > (double(topp) + 1e-6) * Z;
+        if (lane == 0 && !covered) atomicOr(&m->flags, F_OVF);
+      }
+      __syncthreads();
+      if (m->flags & F_OVF) return false;
+    }
+    finalize_keys(c, a, row, topp, sorted, n, n, Z);
+    return true;
+  }
+  // ---- a cluster: this CTA's top-k with ties, then the leader merges ----
+  if (warp == 0) {  // topk_with_ties is warp-synchronous: the whole warp computes it
+    const int nf = topk_with_ties(sorted, min(n, kRankMax), c.K);
+    if (lane == 0) m->n_merge = nf;
+  }
+  cluster.sync();
+  int fl_all = 0, n_all = 0;
+  for (int r = 0; r < CL; ++r) {
+    const Misc* rm = cluster.map_shared_rank(m, r);
+    fl_all |= rm->flags;
+    n_all += rm->n_merge;
+  }
+  const bool hard = (fl_all & (F_NAN | F_TIMEOUT | F_BADID | F_HIST)) != 0;
+  if (!hard && ((fl_all & F_OVF) || n_all > kRankMax)) {  // the multi-pass path, uniformly
+    cluster.sync();
+    if (tid == 0) atomicOr(&m->flags, F_OVF);
+    __syncthreads();
+    return false;
+  }
+  uint64_t* lists = reinterpret_cast<uint64_t*>(c.stages);
+  uint64_t* gsorted = reinterpret_cast<uint64_t*>(c.stages + kRankKeysOff) + kRankMax;
+  int total = 0;
+  if (rank == 0 && !hard) {
+    if (tid == 0) {
+      int t = 0;
+      for (int r = 0; r < CL; ++r) {
+        m->roff[r] = t;
+        t += cluster.map_shared_rank(m, r)->n_merge;
+      }
+      m->roff[CL] = t;
     }
     __syncthreads();
-    if (m->flags & F_OVF) return false;
+    total = m->roff[CL];
+    for (int r = warp; r < CL; r += kWarps) {
+      const uint64_t* src = reinterpret_cast<const uint64_t*>(cluster.map_shared_rank(c.cx, r));
+      for (int i = m->roff[r] + lane; i < m->roff[r + 1]; i += 32) lists[i] = src[i - m->roff[r]];
+    }
   }
-  finalize_keys(c, a, row, topp, sorted, n, n, Z);
+  cluster.sync();  // the leader's reads are done before any CTA exits
+  if (rank != 0) return true;
+  if (hard) {
+    if (tid == 0) a.out_ids[row] = status_from_flags(fl_all, false);
+    return true;
+  }
+  place_sorted_lists(lists, m->roff, CL, total, gsorted);
+  finalize_keys(c, a, row, topp, gsorted, total, total);
   return true;
 }
 
@@ -2884,8 +3015,8 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     softmax_tail(c, a, policy);
     return;
   }
-  if (CL == 1 && mode != MODE_GENERAL && !a.vp_keys) {
-    if (single_block_tail(c, a, mode, ok, s, best, bidx, topp)) return;
+  if (mode != MODE_GENERAL) {
+    if (row_tail(c, a, cluster, CL, rank, mode, ok, s, best, bidx, topp)) return;
     __syncthreads();  // the row continues on the general merge below
   }
   if (fastlike) {  // every warp's final bound; survivors of the tightest
@@ -3015,8 +3146,6 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
 // lies in its own slice's top-k with ties, so the union holds the global set
 // and the result equals the single-device call on the whole row.
 // ---------------------------------------------------------------------------
-constexpr int kMergeStage = kMergeCap;  // union keys the merge stages (32 KB at the stage area's start)
-static_assert(size_t(kMergeStage) * 8 <= kRankKeysOff, "staged lists end before the sorted keys");
 
 struct VpMerge {
   const int64_t* rec;
@@ -3111,27 +3240,7 @@ __global__ void __launch_bounds__(kThreads) vp_merge_kernel(const __grid_constan
     for (int i = lane; i < cnt; i += 32) lists[m->roff[r] + i] = uint64_t(src[i]);
   }
   __syncthreads();
-  for (int e = tid; e < n; e += kThreads) {
-    int r = 0;
-    while (m->roff[r + 1] <= e) ++r;
-    const uint64_t key = lists[e];
-    int pos = e - m->roff[r];
-    for (int r2 = 0; r2 < v.n_ranks; ++r2) {
-      if (r2 == r) continue;
-      const uint64_t* l2 = lists + m->roff[r2];
-      int lo = 0, hi = m->roff[r2 + 1] - m->roff[r2];
-      while (lo < hi) {  // keys of list r2 above `key`
-        const int mid = (lo + hi) >> 1;
-        if (l2[mid] > key)
-          lo = mid + 1;
-        else
-          hi = mid;
-      }
-      pos += lo;
-    }
-    if (pos < kRankMax) sorted[pos] = key;
-  }
-  __syncthreads();
+  place_sorted_lists(lists, m->roff, v.n_ranks, n, sorted);
   finalize_keys(c, a, row, topp, sorted, min(n, kRankMax), n);
 }
 
@@ -3203,9 +3312,9 @@ static int launch(const KArgs& base, int64_t batch, ns_stream_t stream) {
   }
   KArgs a = base;
   const int64_t V = a.vocab;
-  // CTAs per row: enough rows x CTAs to cover the SMs, each warp >= 2 tiles.
+  // CTAs per row: enough rows x CTAs to cover the SMs, each warp >= 1 tile.
   int CL = 1;
-  while (CL < kMaxCluster && batch * CL < di->sms && V / (2 * CL) >= int64_t(kWarps) * 2 * C_::TE) CL *= 2;
+  while (CL < kMaxCluster && batch * CL < di->sms && V / (2 * CL) >= int64_t(kWarps) * C_::TE) CL *= 2;
   int64_t per = (V + CL - 1) / CL;
   per = (per + C_::VE - 1) / C_::VE * C_::VE;
   int64_t pw = (per + kWarps - 1) / kWarps;
