@@ -1045,9 +1045,10 @@ __device__ __forceinline__ void publish_bound(const Ctx<DT>& c, const WarpCand& 
 // before the history prologue; tiles below n_ready were already waited for and
 // masked).  mode: GREEDY or FAST.  Returns false if a bounded wait gave up
 // (F_TIMEOUT is set); in-flight copies are drained first.
-template <int DT>
-__device__ __forceinline__ bool stream_warp(const Ctx<DT>& c, int mode, uint64_t policy, int t_begin, int n_ready,
-                                            WarpCand& s, float& best, int& bidx) {
+// One instantiation per (mode, sign of T) keeps each loop's code compact.
+template <int DT, int MODE, bool NEG>
+__device__ __forceinline__ bool stream_warp_t(const Ctx<DT>& c, uint64_t policy, int t_begin, int n_ready,
+                                              WarpCand& s, float& best, int& bidx) {
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nt = c.wtiles(w);
   const int nfull = full_tiles(c, w);
@@ -1070,26 +1071,17 @@ __device__ __forceinline__ bool stream_warp(const Ctx<DT>& c, int mode, uint64_t
         __syncwarp();
       }
     }
-    if (mode == MODE_GREEDY) {
+    if constexpr (MODE == MODE_GREEDY) {
       greedy_tile(c, w, t, st, best, bidx, t < nfull);
-    } else if (mode == MODE_SOFTMAX) {
-      if (c.neg)
-        mass_tile<DT, true>(c, w, t, st, t < nfull);
-      else
-        mass_tile<DT, false>(c, w, t, st, t < nfull);
-    } else if (!s.ovf) {
-      if (c.neg)
-        fast_tile<DT, true>(c, s, w, t, st, t < nfull);
-      else
-        fast_tile<DT, false>(c, s, w, t, st, t < nfull);
-      if (mode == MODE_NUCLEUS) {
-        if (c.neg)
-          mass_tile<DT, true>(c, w, t, st, t < nfull);
-        else
-          mass_tile<DT, false>(c, w, t, st, t < nfull);
+    } else if constexpr (MODE == MODE_SOFTMAX) {
+      mass_tile<DT, NEG>(c, w, t, st, t < nfull);
+    } else {
+      if (!s.ovf) {
+        fast_tile<DT, NEG>(c, s, w, t, st, t < nfull);
+        if constexpr (MODE == MODE_NUCLEUS) mass_tile<DT, NEG>(c, w, t, st, t < nfull);
+        if (t == 1 || t == 4 || t == 9) publish_bound(c, s);
+        read_shared_tau(c, s);
       }
-      if (t == 1 || t == 4 || t == 9) publish_bound(c, s);
-      read_shared_tau(c, s);
     }
     __syncwarp();
     if (lane == 0 && t + kWStages < nt) {
@@ -1101,6 +1093,23 @@ __device__ __forceinline__ bool stream_warp(const Ctx<DT>& c, int mode, uint64_t
     }
   }
   return true;
+}
+
+template <int DT>
+__device__ __forceinline__ bool stream_warp(const Ctx<DT>& c, int mode, uint64_t policy, int t_begin, int n_ready,
+                                            WarpCand& s, float& best, int& bidx) {
+  switch (mode) {
+    case MODE_GREEDY: return stream_warp_t<DT, MODE_GREEDY, false>(c, policy, t_begin, n_ready, s, best, bidx);
+    case MODE_SOFTMAX:
+      return c.neg ? stream_warp_t<DT, MODE_SOFTMAX, true>(c, policy, t_begin, n_ready, s, best, bidx)
+                   : stream_warp_t<DT, MODE_SOFTMAX, false>(c, policy, t_begin, n_ready, s, best, bidx);
+    case MODE_NUCLEUS:
+      return c.neg ? stream_warp_t<DT, MODE_NUCLEUS, true>(c, policy, t_begin, n_ready, s, best, bidx)
+                   : stream_warp_t<DT, MODE_NUCLEUS, false>(c, policy, t_begin, n_ready, s, best, bidx);
+    default:
+      return c.neg ? stream_warp_t<DT, MODE_FAST, true>(c, policy, t_begin, n_ready, s, best, bidx)
+                   : stream_warp_t<DT, MODE_FAST, false>(c, policy, t_begin, n_ready, s, best, bidx);
+  }
 }
 
 // ---------------------------------------------------------------------------
