@@ -144,6 +144,11 @@ struct Misc {
   uint32_t pub[kWarps];     // FAST: per-warp published bound (key; 0 = none)
   double s_rem;             // SOFTMAX: the draw's remaining mass inside the chosen warp
   int s_warp;               // ... and that warp
+  float nuc_M;              // NUCLEUS: the row's largest scaled value
+  double nuc_Z;             // ... and its total mass sum exp(y - nuc_M)
+  float nuc_yk;             // ... and its kNucleusK-th largest scaled value (-inf: unknown)
+  int w_bin;                // wide NUCLEUS: last bin of the candidate set
+  int w_n;                  // ... its count, and the keys collected
   int roff[kMaxLists + 1];  // leader: union offsets over (rank, warp) lists
   int rc0[kMaxCluster];     // leader: first column of each rank
   uint32_t hist[kBins];
@@ -1076,9 +1081,9 @@ __device__ __forceinline__ bool stream_warp_t(const Ctx<DT>& c, uint64_t policy,
     } else if constexpr (MODE == MODE_SOFTMAX) {
       mass_tile<DT, NEG>(c, w, t, st, t < nfull);
     } else {
+      if (!s.ovf) fast_tile<DT, NEG>(c, s, w, t, st, t < nfull);
+      if constexpr (MODE == MODE_NUCLEUS) mass_tile<DT, NEG>(c, w, t, st, t < nfull);  // even after an overflow
       if (!s.ovf) {
-        fast_tile<DT, NEG>(c, s, w, t, st, t < nfull);
-        if constexpr (MODE == MODE_NUCLEUS) mass_tile<DT, NEG>(c, w, t, st, t < nfull);
         if (t == 1 || t == 4 || t == 9) publish_bound(c, s);
         read_shared_tau(c, s);
       }
@@ -1377,8 +1382,11 @@ __device__ void finalize_small_sorted(const Ctx<DT>& c, const KArgs& a, int64_t 
 // Leader, FAST rows: survivors sorted by (y desc, id asc); softmax; top-p cut
 // (keep sorted j iff j == 0 or cumsum[j-1] <= p, reference sampler.py:122-131);
 // then the inverse-CDF draw over the kept ids in ascending id order.
+// presorted: my[] / mid[] already hold that order.  norm > 0: the softmax's
+// normaliser is the row's total mass (top-k off), not the survivors' sum.
 template <int DT>
-__device__ void finalize_row(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp) {
+__device__ void finalize_row(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, double norm = -1.0,
+                             bool presorted = false) {
   Misc* m = c.m;
   const int tid = threadIdx.x;
   const int n = m->n_merge;
@@ -1389,21 +1397,23 @@ __device__ void finalize_row(const Ctx<DT>& c, const KArgs& a, int64_t row, floa
     if (tid == 0) a.out_ids[row] = NS_ERR_INVALID_DISTRIBUTION;
     return;
   }
-  if (n <= kSmallN) {
+  if (n <= kSmallN && !presorted) {
     finalize_small(c, a, row, topp, n);
     return;
   }
-  int n2 = 1;
-  while (n2 < n) n2 <<= 1;
-  for (int i = tid; i < n2; i += kThreads)
-    keys[i] = (i < n) ? ((uint64_t(f2key(my[i] + 0.0f)) << 32) | uint64_t(~uint32_t(mid[i]))) : 0ull;
-  __syncthreads();
-  bitonic_sort_u64(keys, n2, true);
-  for (int i = tid; i < n; i += kThreads) {
-    my[i] = key2f(uint32_t(keys[i] >> 32));
-    mid[i] = int(~uint32_t(keys[i]));
+  if (!presorted) {
+    int n2 = 1;
+    while (n2 < n) n2 <<= 1;
+    for (int i = tid; i < n2; i += kThreads)
+      keys[i] = (i < n) ? ((uint64_t(f2key(my[i] + 0.0f)) << 32) | uint64_t(~uint32_t(mid[i]))) : 0ull;
+    __syncthreads();
+    bitonic_sort_u64(keys, n2, true);
+    for (int i = tid; i < n; i += kThreads) {
+      my[i] = key2f(uint32_t(keys[i] >> 32));
+      mid[i] = int(~uint32_t(keys[i]));
+    }
+    __syncthreads();
   }
-  __syncthreads();
   const float M = my[0];
   if (!(M < INFINITY)) {
     if (tid == 0) a.out_ids[row] = NS_ERR_INVALID_DISTRIBUTION;
@@ -1418,7 +1428,9 @@ __device__ void finalize_row(const Ctx<DT>& c, const KArgs& a, int64_t row, floa
     const double p = double(topp);
     block_chunk_scan(
         m, n, [&](int i) { return double(my[i]); },
-        [&](int i, double incl, double total) { cnt += (i <= n - 2 && incl <= p * total) ? 1 : 0; });
+        [&](int i, double incl, double total) {
+          cnt += (i <= n - 2 && incl <= p * (norm > 0.0 ? norm : total)) ? 1 : 0;
+        });
     L = 1 + block_sum_int(m, cnt);
   }
   int n3 = 1;
@@ -1633,7 +1645,7 @@ __device__ void finalize_keys(const Ctx<DT>& c, const KArgs& a, int64_t row, flo
   }
   if (tid == 0) m->n_merge = nfin;
   __syncthreads();
-  finalize_row(c, a, row, topp);
+  finalize_row(c, a, row, topp, norm, true);
 }
 
 // Merge nl descending lists of distinct keys (list l at lists[roff[l] ..
@@ -1832,27 +1844,37 @@ __device__ bool row_tail(const Ctx<DT>& c, const KArgs& a, cg::cluster_group& cl
   __syncthreads();
   if (CL == 1) {
     const int fl1 = m->flags;
+    double Z = -1.0;
+    if (nuc) {  // kept for the wide nucleus pass
+      Z = 0.0;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) Z += m->d_red[w];
+      if (tid == 0) {
+        m->nuc_M = M;
+        m->nuc_Z = Z;
+        m->nuc_yk = -INFINITY;
+      }
+    }
     if ((fl1 & (F_OVF | F_BIG)) && !(fl1 & (F_NAN | F_TIMEOUT | F_BADID | F_HIST))) return false;
     const int st = status_from_flags(fl1, false);
     if (st != NS_OK) {
       if (tid == 0) a.out_ids[row] = st;
       return true;
     }
-    double Z = -1.0;
     if (nuc) {
       // the kNucleusK largest with ties must hold more than p of the row's
-      // mass (with a margin above the sums' rounding), else the multi-pass path
-      Z = 0.0;
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) Z += m->d_red[w];
+      // mass (with a margin above the sums' rounding), else a wider pass
       if (warp == 0) {
         const int nfin = topk_with_ties(sorted, n, c.K);
         double cm = 0.0;
         for (int j = lane; j < nfin; j += 32) cm += double(expf(__fsub_rn(key2f(uint32_t(sorted[j] >> 32)), M)));
 #pragma unroll
         for (int o = 16; o; o >>= 1) cm += __shfl_xor_sync(kFull, cm, o);
-        const bool covered = nfin > 0 && nfin <= kSmallN && M > -INFINITY && cm > (double(topp) + 1e-6) * Z;
-        if (lane == 0 && !covered) atomicOr(&m->flags, F_OVF);
+        const bool covered = nfin > 0 && M > -INFINITY && cm > (double(topp) + 1e-6) * Z;
+        if (lane == 0 && !covered) {
+          atomicOr(&m->flags, F_OVF);
+          if (n > 0) m->nuc_yk = key2f(uint32_t(sorted[min(c.K, n) - 1] >> 32));
+        }
       }
       __syncthreads();
       if (m->flags & F_OVF) return false;
@@ -2235,9 +2257,11 @@ __device__ __forceinline__ unsigned long long to_fx(float e) {
 // negated domain when T < 0, col CTA-relative), ft(t) after each tile (all
 // lanes).  `seq` counts the copies this warp has made (it selects ring slots
 // and barrier phases across passes); `pre_issued` tiles were issued already.
+// gmin: the 16-byte groups whose values are all below it (in that domain)
+// are skipped -- fe must ignore every such value.
 template <int DT, class FElem, class FTile>
 __device__ __forceinline__ bool warp_pass(const Ctx<DT>& c, int& seq, int pre_issued, uint64_t policy, float rep,
-                                          float pres, float freq, FElem fe, FTile ft) {
+                                          float pres, float freq, FElem fe, FTile ft, float gmin = -INFINITY) {
   constexpr int VE = Ctx<DT>::VE, TE = Ctx<DT>::TE;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nt = c.wtiles(w);
@@ -2267,8 +2291,13 @@ __device__ __forceinline__ bool warp_pass(const Ctx<DT>& c, int& seq, int pre_is
     const int n_groups = (lead + len + VE - 1) / VE;
     const int colbase = w * c.pw + t * TE - lead;
     for (int q = lane; q < n_groups; q += 32) {
+      const uint4 v = *reinterpret_cast<const uint4*>(st + q * 16);
+      if (gmin > -INFINITY) {  // NaN never skips
+        const float gx = c.neg ? group_extreme<DT, true>(v) : group_extreme<DT, false>(v);
+        if (gx < gmin) continue;
+      }
       float x[VE];
-      unpack16<DT>(*reinterpret_cast<const uint4*>(st + q * 16), x);
+      unpack16<DT>(v, x);
 #pragma unroll
       for (int i = 0; i < VE; ++i) {
         const int e = q * VE + i;
@@ -2334,6 +2363,185 @@ __device__ void cluster_digit(cg::cluster_group& cl, int CL, Misc* m, const unsi
     }
   }
   __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// NUCLEUS rows (one CTA) whose nucleus is larger than the kNucleusK
+// candidates: two more passes over the row instead of the multi-pass path.
+//   A  count the values per bin of d = M - x / |T| (x / |T| rounded through a
+//      reciprocal) over a window [0, D): 2047 bins of D / 2047 nats, deeper
+//      values not counted (no atomic).  D = max(2 dk, dk + 6) nats, dk the
+//      kNucleusK-th largest value's distance from M, at most 32; when the
+//      window holds too little mass, A runs once more with D = 32.  A value in
+//      bin b weighs at least e^-(b+1) D / 2047 (less a margin for the
+//      rounding), so the smallest bin prefix whose guaranteed mass exceeds
+//      (p + 1e-6) Z holds the nucleus (M, Z: the row's largest scaled value and
+//      total mass from the stream).
+//   B  collect the prefix's values as keys (f2key(y) << 32 | ~id) with the
+//      exact y = rn(x / |T|); sort them.
+// The prefix is an upper set of x, so every value scaled above its smallest y
+// is in it; when those values alone hold more than (p + 1e-6) Z (float64
+// sums), the top-p cut lies before the smallest y and the cut and the draw
+// run on the keys with Z as the softmax normaliser (reference
+// sampler.py:122-131, 86-89).  Returns false -- the same on every thread --
+// when the row must continue on the multi-pass path (prefix over kWideCap
+// values, failed check); true when the row's result is written.
+// ---------------------------------------------------------------------------
+constexpr int kWideBins = 2048;
+constexpr float kWideMaxNats = 32.0f;
+constexpr int kWideCap = kCandBytes / 8;  // keys held by the candidate buffers
+static_assert(kWideBins * 4 <= kCandBytes, "the bin counts fit the candidate buffers");
+
+__device__ __forceinline__ int wide_bin(float x, float M, float r, float S) {
+  // explicit roundings: both passes must bin every value identically
+  const float d = __fmul_rn(__fsub_rn(M, __fmul_rn(x, r)), S);
+  return d < float(kWideBins - 1) ? int(fmaxf(d, 0.0f)) : kWideBins - 1;
+}
+
+// A value below this bound lies at least dd nats below M: (M - dd) |T| less
+// a margin far above the few roundings of wide_bin's reciprocal quotient.
+__device__ __forceinline__ float wide_floor(float M, float dd, float Tabs) {
+  const float b = (M - dd) * Tabs;
+  return b - (fabsf(M) + dd) * Tabs * 0x1p-18f - 1e-30f;
+}
+
+template <int DT>
+__device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t policy, float topp) {
+  Misc* m = c.m;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float M = m->nuc_M;
+  const double Z = m->nuc_Z;
+  const float r = __frcp_rn(c.Tabs);
+  uint32_t* h = reinterpret_cast<uint32_t*>(c.cx);
+  uint64_t* keys = reinterpret_cast<uint64_t*>(c.cx);
+  const float dk = __fsub_rn(M, m->nuc_yk);  // +inf when unknown
+  float D = fminf(fmaxf(2.0f * dk, dk + 6.0f), kWideMaxNats);
+  float S = 0.0f;
+  int jb = INT_MAX, nw = 0;
+  for (;;) {
+    S = float(kWideBins - 1) / D;
+    for (int i = tid; i < kWideBins; i += kThreads) h[i] = 0u;
+    if (tid == 0) {
+      m->w_bin = INT_MAX;
+      m->w_n = 0;
+    }
+    __syncthreads();
+    // A: counts per bin
+    warp_pass(
+        c, seq, 0, policy, c.rep, c.pres, c.freq,
+        [&](float x, int) {
+          if (x > -INFINITY) {
+            const int b = wide_bin(x, M, r, S);
+            if (b < kWideBins - 1) atomicAdd(&h[b], 1u);
+          }
+        },
+        [&](int) {}, wide_floor(M, D, c.Tabs));
+    __syncthreads();
+    if (m->flags & F_TIMEOUT) {  // every warp waited for its copies in flight
+      if (tid == 0) a.out_ids[c.row] = NS_ERR_DEVICE_TIMEOUT;
+      return true;
+    }
+    // the smallest prefix of bins whose guaranteed mass exceeds the target
+    constexpr int per = kWideBins / kThreads;
+    const float wb = D / float(kWideBins - 1);  // nats per bin
+    int cnt[per];
+    double lm = 0.0;
+    int lc = 0;
+#pragma unroll
+    for (int k = 0; k < per; ++k) {
+      const int b = tid * per + k;
+      cnt[k] = int(h[b]);
+      lc += cnt[k];
+      lm += double(cnt[k]) * double(expf(-(float(b) + 1.0f) * wb - 1e-4f));
+    }
+    double im = lm;
+    int ic = lc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double vm = __shfl_up_sync(kFull, im, o);
+      const int vc = __shfl_up_sync(kFull, ic, o);
+      if (lane >= o) {
+        im += vm;
+        ic += vc;
+      }
+    }
+    if (lane == 31) {
+      m->d_red[warp] = im;
+      m->i_red[warp] = ic;
+    }
+    __syncthreads();
+    double runm = im - lm;
+    int runc = ic - lc;
+    for (int w = 0; w < warp; ++w) {
+      runm += m->d_red[w];
+      runc += m->i_red[w];
+    }
+    const double target = (double(topp) + 1e-6) * Z;
+#pragma unroll
+    for (int k = 0; k < per; ++k) {
+      const int b = tid * per + k;
+      const bool before = runm > target;
+      runm += double(cnt[k]) * double(expf(-(float(b) + 1.0f) * wb - 1e-4f));
+      runc += cnt[k];
+      if (!before && runm > target) {  // one thread at most
+        m->w_bin = b;
+        m->w_n = runc;
+      }
+    }
+    __syncthreads();
+    jb = m->w_bin;
+    nw = m->w_n;
+    __syncthreads();
+    if (jb != INT_MAX || D >= kWideMaxNats) break;
+    D = kWideMaxNats;  // the window held too little mass: once more, wider
+  }
+  if (jb == INT_MAX || nw > kWideCap || nw == 0) return false;
+  if (tid == 0) m->w_n = 0;
+  __syncthreads();
+  // B: collect the prefix (the bin counts are dead)
+  warp_pass(
+      c, seq, 0, policy, c.rep, c.pres, c.freq,
+      [&](float x, int col) {
+        if (x > -INFINITY && wide_bin(x, M, r, S) <= jb) {
+          const float y = __fdiv_rn(x, c.Tabs) + 0.0f;  // -0 and +0 tie
+          const int i = atomicAdd(&m->w_n, 1);
+          if (i < kWideCap) keys[i] = (uint64_t(f2key(y)) << 32) | uint64_t(~uint32_t(c.c0 + col));
+        }
+      },
+      [&](int) {}, wide_floor(M, float(jb + 1) / S, c.Tabs));
+  __syncthreads();
+  if (m->flags & F_TIMEOUT) {
+    if (tid == 0) a.out_ids[c.row] = NS_ERR_DEVICE_TIMEOUT;
+    return true;
+  }
+  const int n = m->w_n;
+  if (n > kWideCap || n == 0) return false;
+  int n2 = 1;
+  while (n2 < n) n2 <<= 1;
+  for (int i = n + tid; i < n2; i += kThreads) keys[i] = 0ull;
+  __syncthreads();
+  bitonic_sort_u64(keys, n2, true);
+  // exact mass of the keys above the smallest scaled value
+  {
+    const uint32_t ylast = uint32_t(keys[n - 1] >> 32);
+    double cm = 0.0;
+    for (int i = tid; i < n; i += kThreads) {
+      const uint32_t yk = uint32_t(keys[i] >> 32);
+      if (yk > ylast) cm += double(expf(__fsub_rn(key2f(yk), M)));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) cm += __shfl_xor_sync(kFull, cm, o);
+    if (lane == 0) m->d_red[warp] = cm;
+    __syncthreads();
+    double tot = 0.0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) tot += m->d_red[w];
+    __syncthreads();
+    if (!(tot > (double(topp) + 1e-6) * Z) || key2f(uint32_t(keys[0] >> 32)) != M) return false;
+  }
+  c.K = n;  // no top-k: every key is a survivor
+  finalize_keys(c, a, c.row, topp, keys, n, n, Z);
+  return true;
 }
 
 template <int DT>
@@ -3024,9 +3232,11 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     softmax_tail(c, a, policy);
     return;
   }
+  int seq_next = c.wtiles(warp);  // copies this warp has made
   if (mode != MODE_GENERAL) {
     if (row_tail(c, a, cluster, CL, rank, mode, ok, s, best, bidx, topp)) return;
-    __syncthreads();  // the row continues on the general merge below
+    __syncthreads();  // the row continues below
+    if (mode == MODE_NUCLEUS && nucleus_wide(c, a, seq_next, policy, topp)) return;  // one CTA
   }
   if (fastlike) {  // every warp's final bound; survivors of the tightest
     if (ok) publish_bound(c, s);
@@ -3085,7 +3295,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
       c.K = topk;  // NUCLEUS rows filtered with kNucleusK
       if (tid == 0) m->flags &= ~F_OVF;
       __syncthreads();
-      int seq = (mode == MODE_GENERAL) ? 0 : c.wtiles(warp);
+      int seq = (mode == MODE_GENERAL) ? 0 : seq_next;
       const int pre = (mode == MODE_GENERAL) ? min(kWStages, c.wtiles(warp)) : 0;
       general_row(c, a, cluster, CL, rank, seq, pre, policy, rep, pres, freq, topp);
       return;

@@ -187,11 +187,13 @@ def test_tie_plateau_merge_paths(sampler, n_ties, K, B):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_softmax_rows_top_k_and_top_p_off(sampler, dtype):
+@pytest.mark.parametrize("B", [96, 160])
+def test_softmax_rows_top_k_and_top_p_off(sampler, dtype, B):
     """The reference's default request (top_k -1, top_p 1.0): the draw is over
-    the whole softmax.  96 full-size rows run one block per row (the one-pass
-    softmax path); k 0 or >= V and p 0.0 also disable the filters."""
-    B, V = 96, 151936
+    the whole softmax.  160 full-size rows (more than the SMs) run one block
+    per row -- the one-pass softmax path; 96 rows run 2-block clusters -- the
+    multi-pass path.  k 0 or >= V and p 0.0 also disable the filters."""
+    V = 151936
     x = make_logits(61, B, V, 3.0, spike_frac=0.005, dtype=dtype)
     hs = make_histories(62, B, V, 256)
     rng = np.random.default_rng(63)
@@ -213,11 +215,14 @@ def test_softmax_rows_top_k_and_top_p_off(sampler, dtype):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_nucleus_rows_top_k_off(sampler, dtype):
-    """Top-k off with top-p on: the one-pass path keeps the 128 largest as
-    candidates and checks they hold more than p of the row's mass; rows whose
-    nucleus is larger (a flat row, a wide plateau) take the multi-pass path."""
-    B, V = 96, 151936
+@pytest.mark.parametrize("B", [96, 160])
+def test_nucleus_rows_top_k_off(sampler, dtype, B):
+    """Top-k off with top-p on.  One block per row (160 rows): the stream keeps
+    the 128 largest as candidates and checks they hold more than p of the
+    row's mass; larger nuclei take two more passes (a plateau of 300 near-equal
+    leaders), and a nucleus past the key capacity (a flat row) the multi-pass
+    path.  Clusters (96 rows) take the multi-pass path."""
+    V = 151936
     x = make_logits(71, B, V, 3.0, spike_frac=0.005, dtype=torch.float32)
     x[7] = torch.randn(V, generator=torch.Generator().manual_seed(7)) * 0.01    # nucleus ~ 0.9 V
     x[9, :300] = 8.0 + torch.arange(300, dtype=torch.float32) * 1e-3            # ~300 near-equal leaders
@@ -235,6 +240,35 @@ def test_nucleus_rows_top_k_off(sampler, dtype):
     u = make_uniforms(74, B)
     ids, ref = run(sampler, x, hs, params, u)
     assert check(ids, ref, f"nucleus {dtype}") <= 3
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_wide_nucleus_rows(sampler, dtype):
+    """Top-p only, nuclei of a few hundred to a few thousand values (one block
+    per row): the bin-count pass and the key pass, with ties straddling the
+    candidate set's last bin, penalised history columns inside the nucleus,
+    negative temperatures; nuclei past the key capacity take the multi-pass
+    path."""
+    B, V = 160, 151936
+    x = make_logits(81, B, V, 3.0, dtype=torch.float32)
+    top = x.max(dim=1).values
+    for b in range(0, B, 10):       # a plateau of ~1500 equal values a few nats below the max
+        x[b, b % 7::97] = top[b] - 3.0 - 0.01 * (b % 13)
+    for b in range(3, B, 10):       # a narrow band of near-equal values
+        x[b, 5000:5600] = top[b] - 2.0 + torch.arange(600, dtype=torch.float32) * 1e-4
+    x = x.to(dtype)
+    hs = make_histories(82, B, V, 512)
+    for b in range(3, B, 10):       # history ids inside the band
+        hs[b] = hs[b] + list(range(5000, 5600, 7))
+    rng = np.random.default_rng(83)
+    params = []
+    for b in range(B):
+        pen = dict(repetition_penalty=1.1, presence_penalty=0.3, frequency_penalty=0.1) if b % 2 else {}
+        params.append(SamplingParams(temperature=float(rng.choice([0.5, 0.7, 1.0, -0.8, 1.3])),
+                                     top_k=-1, top_p=float(rng.choice([0.6, 0.8, 0.9, 0.95, 0.99])), **pen))
+    u = make_uniforms(84, B)
+    ids, ref = run(sampler, x, hs, params, u)
+    assert check(ids, ref, f"wide nucleus {dtype}") <= 8
 
 
 def test_philox_default_stream_matches_oracle(sampler):
