@@ -1255,6 +1255,8 @@ __device__ __forceinline__ int status_from_flags(int f, bool greedy) {
 }
 
 constexpr int kSmallN = 128;
+constexpr int kSmallRank = 2048;  // finalise: kept sets up to this size are ordered by rank counting
+static_assert(kSmallRank + 3 <= kMergeCap, "rank counting reads whole int4s of the merge ids");
 
 template <int DT>
 __device__ void finalize_small_sorted(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, int n,
@@ -1433,12 +1435,26 @@ __device__ void finalize_row(const Ctx<DT>& c, const KArgs& a, int64_t row, floa
         });
     L = 1 + block_sum_int(m, cnt);
   }
-  int n3 = 1;
-  while (n3 < L) n3 <<= 1;
-  for (int i = tid; i < n3; i += kThreads)
-    keys[i] = (i < L) ? ((uint64_t(uint32_t(mid[i])) << 32) | uint64_t(__float_as_uint(my[i]))) : ~0ull;
-  __syncthreads();
-  bitonic_sort_u64(keys, n3, false);
+  if (L <= kSmallRank) {  // ascending id by rank counting (ids are distinct)
+    for (int i = tid; i < L; i += kThreads) {
+      const int idi = mid[i];
+      int rk = 0;
+      for (int j = 0; j < L; j += 4) {  // mid[] holds merge_cap >= L + 3 entries
+        const int4 q = *reinterpret_cast<const int4*>(mid + j);
+        rk += (q.x < idi ? 1 : 0) + (j + 1 < L && q.y < idi ? 1 : 0) + (j + 2 < L && q.z < idi ? 1 : 0) +
+              (j + 3 < L && q.w < idi ? 1 : 0);
+      }
+      keys[rk] = (uint64_t(uint32_t(idi)) << 32) | uint64_t(__float_as_uint(my[i]));
+    }
+    __syncthreads();
+  } else {
+    int n3 = 1;
+    while (n3 < L) n3 <<= 1;
+    for (int i = tid; i < n3; i += kThreads)
+      keys[i] = (i < L) ? ((uint64_t(uint32_t(mid[i])) << 32) | uint64_t(__float_as_uint(my[i]))) : ~0ull;
+    __syncthreads();
+    bitonic_sort_u64(keys, n3, false);
+  }
   const float u = a.uniforms ? c.u_pre : philox_uniform(a.seed, a.offset, uint64_t(row));
   if (tid == 0) m->choose = INT_MAX;
   __syncthreads();
@@ -2253,12 +2269,24 @@ __device__ __forceinline__ unsigned long long to_fx(float e) {
   return (unsigned long long)(double(e) * kFx);
 }
 
+// A bound below every x (same domain) with rn(x / Tabs) >= ylo: ylo * Tabs
+// less a relative margin far above one quotient rounding and an absolute one
+// above the subnormal spacing (a pass's 16-byte-group skip; -inf: none).
+__device__ __forceinline__ float x_floor_of_y(float ylo, float Tabs) {
+  if (!(ylo > -INFINITY)) return -INFINITY;  // -inf or NaN: no bound
+  const double b = double(ylo) * double(Tabs);
+  return __double2float_rd(b - fabs(b) * 0x1p-20 - double(Tabs) * 0x1p-120);
+}
+
 // One pass of this warp over its tiles: fe(x, col) for every value (x in the
 // negated domain when T < 0, col CTA-relative), ft(t) after each tile (all
 // lanes).  `seq` counts the copies this warp has made (it selects ring slots
 // and barrier phases across passes); `pre_issued` tiles were issued already.
 // gmin: the 16-byte groups whose values are all below it (in that domain)
-// are skipped -- fe must ignore every such value.
+// are skipped -- fe must ignore every such value.  Each lane then marks its
+// groups that reach gmin and the warp works through them one group per lane
+// per round, so a sparse set of hot groups costs a few rounds, not a full
+// divergent sweep.
 template <int DT, class FElem, class FTile>
 __device__ __forceinline__ bool warp_pass(const Ctx<DT>& c, int& seq, int pre_issued, uint64_t policy, float rep,
                                           float pres, float freq, FElem fe, FTile ft, float gmin = -INFINITY) {
@@ -2290,18 +2318,35 @@ __device__ __forceinline__ bool warp_pass(const Ctx<DT>& c, int& seq, int pre_is
     const int len = c.tile_len(w, t), lead = c.tile_lead(w, t);
     const int n_groups = (lead + len + VE - 1) / VE;
     const int colbase = w * c.pw + t * TE - lead;
-    for (int q = lane; q < n_groups; q += 32) {
-      const uint4 v = *reinterpret_cast<const uint4*>(st + q * 16);
-      if (gmin > -INFINITY) {  // NaN never skips
+    if (gmin > -INFINITY) {
+      unsigned gm = 0;  // bit k: group k * 32 + lane reaches gmin (or holds NaN)
+      for (int k = 0; k * 32 + lane < n_groups; ++k) {
+        const uint4 v = *reinterpret_cast<const uint4*>(st + (k * 32 + lane) * 16);
         const float gx = c.neg ? group_extreme<DT, true>(v) : group_extreme<DT, false>(v);
-        if (gx < gmin) continue;
+        gm |= (gx < gmin ? 0u : 1u) << k;
       }
-      float x[VE];
-      unpack16<DT>(v, x);
+      while (__any_sync(kFull, gm != 0u)) {
+        if (gm) {
+          const int q = (__ffs(gm) - 1) * 32 + lane;
+          gm &= gm - 1u;
+          float x[VE];
+          unpack16<DT>(*reinterpret_cast<const uint4*>(st + q * 16), x);
 #pragma unroll
-      for (int i = 0; i < VE; ++i) {
-        const int e = q * VE + i;
-        if (e >= lead && e < lead + len) fe(c.neg ? -x[i] : x[i], colbase + e);
+          for (int i = 0; i < VE; ++i) {
+            const int e = q * VE + i;
+            if (e >= lead && e < lead + len) fe(c.neg ? -x[i] : x[i], colbase + e);
+          }
+        }
+      }
+    } else {
+      for (int q = lane; q < n_groups; q += 32) {
+        float x[VE];
+        unpack16<DT>(*reinterpret_cast<const uint4*>(st + q * 16), x);
+#pragma unroll
+        for (int i = 0; i < VE; ++i) {
+          const int e = q * VE + i;
+          if (e >= lead && e < lead + len) fe(c.neg ? -x[i] : x[i], colbase + e);
+        }
       }
     }
     ft(t);
@@ -2370,9 +2415,10 @@ __device__ void cluster_digit(cg::cluster_group& cl, int CL, Misc* m, const unsi
 // candidates: two more passes over the row instead of the multi-pass path.
 //   A  count the values per bin of d = M - x / |T| (x / |T| rounded through a
 //      reciprocal) over a window [0, D): 2047 bins of D / 2047 nats, deeper
-//      values not counted (no atomic).  D = max(2 dk, dk + 6) nats, dk the
-//      kNucleusK-th largest value's distance from M, at most 32; when the
-//      window holds too little mass, A runs once more with D = 32.  A value in
+//      values not counted (and their 16-byte groups skipped).  D = dk + 4
+//      nats, dk the kNucleusK-th largest value's distance from M, at most 32;
+//      while the window holds too little mass, A runs again with D doubled
+//      (at most 32).  A value in
 //      bin b weighs at least e^-(b+1) D / 2047 (less a margin for the
 //      rounding), so the smallest bin prefix whose guaranteed mass exceeds
 //      (p + 1e-6) Z holds the nucleus (M, Z: the row's largest scaled value and
@@ -2415,7 +2461,7 @@ __device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t poli
   uint32_t* h = reinterpret_cast<uint32_t*>(c.cx);
   uint64_t* keys = reinterpret_cast<uint64_t*>(c.cx);
   const float dk = __fsub_rn(M, m->nuc_yk);  // +inf when unknown
-  float D = fminf(fmaxf(2.0f * dk, dk + 6.0f), kWideMaxNats);
+  float D = fminf(dk + 4.0f, kWideMaxNats);
   float S = 0.0f;
   int jb = INT_MAX, nw = 0;
   for (;;) {
@@ -2493,7 +2539,7 @@ __device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t poli
     nw = m->w_n;
     __syncthreads();
     if (jb != INT_MAX || D >= kWideMaxNats) break;
-    D = kWideMaxNats;  // the window held too little mass: once more, wider
+    D = fminf(2.0f * D, kWideMaxNats);  // the window held too little mass: wider
   }
   if (jb == INT_MAX || nw > kWideCap || nw == 0) return false;
   if (tid == 0) m->w_n = 0;
@@ -2632,7 +2678,7 @@ __device__ void general_row(const Ctx<DT>& c, const KArgs& a, cg::cluster_group&
             const uint32_t k = f2key(x);
             if (x > -INFINITY && x == x && (k >> 21) == uint32_t(d0)) atomicAdd(&gh[(k >> 10) & 0x7FFu], 1ull);
           },
-          [&](int) {});
+          [&](int) {}, key2f(uint32_t(d0) << 21));
       __syncthreads();
       cl.sync();
       cluster_digit(cl, CL, m, gh, kGBins, krem, false);
@@ -2648,7 +2694,7 @@ __device__ void general_row(const Ctx<DT>& c, const KArgs& a, cg::cluster_group&
             const uint32_t k = f2key(x);
             if (x > -INFINITY && x == x && (k >> 10) == pre) atomicAdd(&gh[k & 0x3FFu], 1ull);
           },
-          [&](int) {});
+          [&](int) {}, key2f(pre << 10));
       __syncthreads();
       cl.sync();
       cluster_digit(cl, CL, m, gh, 1024, krem, false);
@@ -2677,7 +2723,8 @@ __device__ void general_row(const Ctx<DT>& c, const KArgs& a, cg::cluster_group&
           const unsigned long long sum = warp_sum_u64(acc);
           acc = 0;
           if (lane == 0) tmass[warp * c.tpw + t] = sum;
-        });
+        },
+        lo);
   }
   __syncthreads();
   if (tid == 0) {
@@ -2713,7 +2760,7 @@ __device__ void general_row(const Ctx<DT>& c, const KArgs& a, cg::cluster_group&
             const uint32_t k = f2key(y + 0.0f);
             if ((k >> 21) == uint32_t(b0)) atomicAdd(&gh[(k >> 10) & 0x7FFu], to_fx(expf(__fsub_rn(y, M))));
           },
-          [&](int) {});
+          [&](int) {}, fmaxf(lo, x_floor_of_y(key2f(uint32_t(b0) << 21), c.Tabs)));
       __syncthreads();
       cl.sync();
       cluster_digit(cl, CL, m, gh, kGBins, target0 - O, true);
@@ -2731,7 +2778,7 @@ __device__ void general_row(const Ctx<DT>& c, const KArgs& a, cg::cluster_group&
             const uint32_t k = f2key(y + 0.0f);
             if ((k >> 10) == pre) atomicAdd(&gh[k & 0x3FFu], to_fx(expf(__fsub_rn(y, M))));
           },
-          [&](int) {});
+          [&](int) {}, fmaxf(lo, x_floor_of_y(key2f(pre << 10), c.Tabs)));
       __syncthreads();
       cl.sync();
       cluster_digit(cl, CL, m, gh, 1024, target0 - O, true);
@@ -2767,7 +2814,8 @@ __device__ void general_row(const Ctx<DT>& c, const KArgs& a, cg::cluster_group&
                 tmass[warp * c.tpw + t] = sum;
                 tties[warp * c.tpw + t] = tt;
               }
-            });
+            },
+            fmaxf(lo, x_floor_of_y(cval, c.Tabs)));
       }
       __syncthreads();
       if (tid == 0) {
