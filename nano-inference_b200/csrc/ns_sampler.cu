@@ -149,6 +149,7 @@ struct Misc {
   float nuc_yk;             // ... and its kNucleusK-th largest scaled value (-inf: unknown)
   int w_bin;                // wide NUCLEUS: last bin of the candidate set
   int w_n;                  // ... its count, and the keys collected
+  int w_tot;                // ... values counted in the window
   int roff[kMaxLists + 1];  // leader: union offsets over (rank, warp) lists
   int rc0[kMaxCluster];     // leader: first column of each rank
   uint32_t hist[kBins];
@@ -1243,6 +1244,50 @@ __device__ int block_sum_int(Misc* m, int v) {
   return s;
 }
 
+// Orders n distinct keys by before(a, b) into out[]: counted into kBins
+// buckets (shared atomics), placed by bucket into tmp[], then ranked inside
+// their bucket.  bucket(k) in [0, kBins) must follow the order: bucket(a) <
+// bucket(b) implies before(a, b).  O(n) plus the squares of the bucket sizes.
+// Uses Misc::hist and Misc::i_red; all threads of the block; a barrier follows.
+template <class Bucket, class Before>
+__device__ void bucket_sort(Misc* m, const uint64_t* in, int n, uint64_t* tmp, uint64_t* out, Bucket bucket,
+                            Before before) {
+  static_assert(kBins == kThreads, "one bucket per thread in the scan");
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint32_t* cnt = m->hist;
+  cnt[tid] = 0u;
+  __syncthreads();
+  for (int i = tid; i < n; i += kThreads) atomicAdd(&cnt[bucket(in[i])], 1u);
+  __syncthreads();
+  const int v = int(cnt[tid]);
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(kFull, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) m->i_red[warp] = incl;
+  __syncthreads();
+  int base = 0;
+  for (int w = 0; w < warp; ++w) base += m->i_red[w];
+  cnt[tid] = uint32_t(base + incl - v);  // first slot of bucket tid
+  __syncthreads();
+  for (int i = tid; i < n; i += kThreads) {
+    const uint64_t k = in[i];
+    tmp[atomicAdd(&cnt[bucket(k)], 1u)] = k;
+  }
+  __syncthreads();  // cnt[b]: one past the last slot of bucket b
+  for (int p = tid; p < n; p += kThreads) {
+    const uint64_t k = tmp[p];
+    const int b = bucket(k);
+    const int s0 = b ? int(cnt[b - 1]) : 0, s1 = int(cnt[b]);
+    int r = 0;
+    for (int q = s0; q < s1; ++q) r += before(tmp[q], k) ? 1 : 0;
+    out[s0 + r] = k;
+  }
+  __syncthreads();
+}
+
 __device__ __forceinline__ int status_from_flags(int f, bool greedy) {
   if (f & F_TIMEOUT) return NS_ERR_DEVICE_TIMEOUT;
   if (f & F_BADID) return NS_ERR_TOKEN_ID_OUT_OF_RANGE;
@@ -1255,8 +1300,8 @@ __device__ __forceinline__ int status_from_flags(int f, bool greedy) {
 }
 
 constexpr int kSmallN = 128;
-constexpr int kSmallRank = 2048;  // finalise: kept sets up to this size are ordered by rank counting
-static_assert(kSmallRank + 3 <= kMergeCap, "rank counting reads whole int4s of the merge ids");
+constexpr int kSmallRank = 2048;  // finalise: kept sets up to this size are bucket-sorted by id
+static_assert(2 * kSmallRank <= kMergeCap, "the id keys and their bucket staging fit the finalise keys area");
 
 template <int DT>
 __device__ void finalize_small_sorted(const Ctx<DT>& c, const KArgs& a, int64_t row, float topp, int n,
@@ -1435,18 +1480,19 @@ __device__ void finalize_row(const Ctx<DT>& c, const KArgs& a, int64_t row, floa
         });
     L = 1 + block_sum_int(m, cnt);
   }
-  if (L <= kSmallRank) {  // ascending id by rank counting (ids are distinct)
-    for (int i = tid; i < L; i += kThreads) {
-      const int idi = mid[i];
-      int rk = 0;
-      for (int j = 0; j < L; j += 4) {  // mid[] holds merge_cap >= L + 3 entries
-        const int4 q = *reinterpret_cast<const int4*>(mid + j);
-        rk += (q.x < idi ? 1 : 0) + (j + 1 < L && q.y < idi ? 1 : 0) + (j + 2 < L && q.z < idi ? 1 : 0) +
-              (j + 3 < L && q.w < idi ? 1 : 0);
-      }
-      keys[rk] = (uint64_t(uint32_t(idi)) << 32) | uint64_t(__float_as_uint(my[i]));
-    }
+  const uint64_t* ord = keys;  // (id << 32 | weight) in ascending id order
+  if (L <= kSmallRank) {  // bucket sort by id range (ids are distinct)
+    for (int i = tid; i < L; i += kThreads)
+      keys[i] = (uint64_t(uint32_t(mid[i])) << 32) | uint64_t(__float_as_uint(my[i]));
     __syncthreads();
+    int sh = 0;  // ids < vocab_total <= 2^(8 + sh)
+    while ((a.vocab_total - 1) >> (8 + sh)) ++sh;
+    uint64_t* tmp = keys + kSmallRank;
+    uint64_t* out = reinterpret_cast<uint64_t*>(my);  // my[] and mid[] are dead
+    bucket_sort(
+        m, keys, L, tmp, out, [&](uint64_t k) { return int(uint32_t(k >> 32) >> sh); },
+        [](uint64_t x, uint64_t y) { return x < y; });
+    ord = out;
   } else {
     int n3 = 1;
     while (n3 < L) n3 <<= 1;
@@ -1460,7 +1506,7 @@ __device__ void finalize_row(const Ctx<DT>& c, const KArgs& a, int64_t row, floa
   __syncthreads();
   int first = INT_MAX;
   block_chunk_scan(
-      m, L, [&](int i) { return double(__uint_as_float(uint32_t(keys[i]))); },
+      m, L, [&](int i) { return double(__uint_as_float(uint32_t(ord[i]))); },
       [&](int i, double incl, double total) {
         if (first == INT_MAX && incl > double(u) * total) first = i;
       });
@@ -1468,7 +1514,7 @@ __device__ void finalize_row(const Ctx<DT>& c, const KArgs& a, int64_t row, floa
   __syncthreads();
   if (tid == 0) {
     const int ch = (m->choose == INT_MAX) ? L - 1 : m->choose;
-    a.out_ids[row] = int64_t(uint32_t(keys[ch] >> 32)) + a.vocab_offset;
+    a.out_ids[row] = int64_t(uint32_t(ord[ch] >> 32)) + a.vocab_offset;
   }
 }
 
@@ -2412,34 +2458,39 @@ __device__ void cluster_digit(cg::cluster_group& cl, int CL, Misc* m, const unsi
 
 // ---------------------------------------------------------------------------
 // NUCLEUS rows (one CTA) whose nucleus is larger than the kNucleusK
-// candidates: two more passes over the row instead of the multi-pass path.
-//   A  count the values per bin of d = M - x / |T| (x / |T| rounded through a
-//      reciprocal) over a window [0, D): 2047 bins of D / 2047 nats, deeper
-//      values not counted (and their 16-byte groups skipped).  D = dk + 4
-//      nats, dk the kNucleusK-th largest value's distance from M, at most 32;
-//      while the window holds too little mass, A runs again with D doubled
-//      (at most 32).  A value in
-//      bin b weighs at least e^-(b+1) D / 2047 (less a margin for the
-//      rounding), so the smallest bin prefix whose guaranteed mass exceeds
-//      (p + 1e-6) Z holds the nucleus (M, Z: the row's largest scaled value and
-//      total mass from the stream).
-//   B  collect the prefix's values as keys (f2key(y) << 32 | ~id) with the
-//      exact y = rn(x / |T|); sort them.
-// The prefix is an upper set of x, so every value scaled above its smallest y
-// is in it; when those values alone hold more than (p + 1e-6) Z (float64
-// sums), the top-p cut lies before the smallest y and the cut and the draw
-// run on the keys with Z as the softmax normaliser (reference
-// sampler.py:122-131, 86-89).  Returns false -- the same on every thread --
-// when the row must continue on the multi-pass path (prefix over kWideCap
-// values, failed check); true when the row's result is written.
+// candidates.  One more pass over the row counts the values within D nats of
+// M in 255 bins of D / 255 nats (d = M - x / |T| through a reciprocal; deeper
+// values, and 16-byte groups holding only such values, are skipped) and
+// collects those of the first kb bins as keys (f2key(y) << 32 | ~id, y =
+// rn(x / |T|)).  M, Z: the row's largest scaled value and total mass from the
+// stream; D = dk + 4.5 and the keys' window dk + 3.5 nats, dk the kNucleusK-th
+// largest value's distance from M.  A value in bin b weighs at least
+// e^-(b+1) D / 255 (less a margin for the rounding), so the smallest bin
+// prefix whose guaranteed mass exceeds (p + 1e-6) Z holds the nucleus.  No
+// such prefix: the pass repeats with D doubled (at most 32 nats) and keys from
+// every bin (unless the window already counts more than kWideCap values).  A
+// prefix past the keys' bins, or more than kWideCap keys: one more pass
+// collects that prefix alone.
+// The collected set is an upper set of x, so every value scaled above its
+// smallest y is in it; the keys are sorted (by bucket of y, then rank), and
+// when those values alone hold more than (p + 1e-6) Z (float64 sums) the
+// top-p cut lies before the smallest y: the cut and the draw run on the keys
+// with Z as the softmax normaliser (reference sampler.py:122-131, 86-89).
+// Returns false -- the same on every thread -- when the row continues on the
+// multi-pass path (prefix over kWideCap values, failed check); true when its
+// result is written.
 // ---------------------------------------------------------------------------
-constexpr int kWideBins = 2048;
+constexpr int kWideBins = kBins;  // 255 window bins + the deeper values
 constexpr float kWideMaxNats = 32.0f;
 constexpr int kWideCap = kCandBytes / 8;  // keys held by the candidate buffers
-static_assert(kWideBins * 4 <= kCandBytes, "the bin counts fit the candidate buffers");
+static_assert(kWideBins == kThreads, "one bin per thread in the prefix scan");
+static_assert(size_t(kMergeCap + kWideCap) * 8 <= kRankKeysOff + size_t(kRankMax) * 8,
+              "the bucket staging ends where the sorted keys start");
+static_assert(kRankKeysOff + size_t(kRankMax + kWideCap) * 8 <= size_t(kStageBytes),
+              "the sorted window keys fit the stage area");
 
 __device__ __forceinline__ int wide_bin(float x, float M, float r, float S) {
-  // explicit roundings: both passes must bin every value identically
+  // explicit roundings: every pass bins a value identically
   const float d = __fmul_rn(__fsub_rn(M, __fmul_rn(x, r)), S);
   return d < float(kWideBins - 1) ? int(fmaxf(d, 0.0f)) : kWideBins - 1;
 }
@@ -2458,27 +2509,37 @@ __device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t poli
   const float M = m->nuc_M;
   const double Z = m->nuc_Z;
   const float r = __frcp_rn(c.Tabs);
-  uint32_t* h = reinterpret_cast<uint32_t*>(c.cx);
+  uint32_t* h = m->hist;
   uint64_t* keys = reinterpret_cast<uint64_t*>(c.cx);
+  auto key_of = [&](float x, int col) {
+    const float y = __fdiv_rn(x, c.Tabs) + 0.0f;  // -0 and +0 tie
+    return (uint64_t(f2key(y)) << 32) | uint64_t(~uint32_t(c.c0 + col));
+  };
   const float dk = __fsub_rn(M, m->nuc_yk);  // +inf when unknown
-  float D = fminf(dk + 4.0f, kWideMaxNats);
+  float D = fminf(dk + 4.5f, kWideMaxNats);
   float S = 0.0f;
-  int jb = INT_MAX, nw = 0;
-  for (;;) {
+  int jb = INT_MAX, nb = 0, n = 0, kb = 0;
+  for (int att = 0;; ++att) {
     S = float(kWideBins - 1) / D;
-    for (int i = tid; i < kWideBins; i += kThreads) h[i] = 0u;
+    kb = (att == 0) ? int(fminf((dk + 3.5f) * S, float(kWideBins - 1))) : kWideBins - 1;  // NaN: all
+    h[tid] = 0u;
     if (tid == 0) {
       m->w_bin = INT_MAX;
       m->w_n = 0;
     }
     __syncthreads();
-    // A: counts per bin
     warp_pass(
         c, seq, 0, policy, c.rep, c.pres, c.freq,
-        [&](float x, int) {
+        [&](float x, int col) {
           if (x > -INFINITY) {
             const int b = wide_bin(x, M, r, S);
-            if (b < kWideBins - 1) atomicAdd(&h[b], 1u);
+            if (b < kWideBins - 1) {
+              atomicAdd(&h[b], 1u);
+              if (b < kb) {
+                const int i = atomicAdd(&m->w_n, 1);
+                if (i < kWideCap) keys[i] = key_of(x, col);
+              }
+            }
           }
         },
         [&](int) {}, wide_floor(M, D, c.Tabs));
@@ -2487,21 +2548,12 @@ __device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t poli
       if (tid == 0) a.out_ids[c.row] = NS_ERR_DEVICE_TIMEOUT;
       return true;
     }
+    n = m->w_n;
     // the smallest prefix of bins whose guaranteed mass exceeds the target
-    constexpr int per = kWideBins / kThreads;
-    const float wb = D / float(kWideBins - 1);  // nats per bin
-    int cnt[per];
-    double lm = 0.0;
-    int lc = 0;
-#pragma unroll
-    for (int k = 0; k < per; ++k) {
-      const int b = tid * per + k;
-      cnt[k] = int(h[b]);
-      lc += cnt[k];
-      lm += double(cnt[k]) * double(expf(-(float(b) + 1.0f) * wb - 1e-4f));
-    }
+    const int cnt = (tid < kWideBins - 1) ? int(h[tid]) : 0;
+    const double lm = double(cnt) * double(expf(-(float(tid) + 1.0f) * (D / float(kWideBins - 1)) - 1e-4f));
     double im = lm;
-    int ic = lc;
+    int ic = cnt;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const double vm = __shfl_up_sync(kFull, im, o);
@@ -2516,63 +2568,62 @@ __device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t poli
       m->i_red[warp] = ic;
     }
     __syncthreads();
-    double runm = im - lm;
-    int runc = ic - lc;
-    for (int w = 0; w < warp; ++w) {
-      runm += m->d_red[w];
-      runc += m->i_red[w];
+    for (int w = 0; w < warp; ++w) {  // never reads the last warp's entries
+      im += m->d_red[w];
+      ic += m->i_red[w];
     }
     const double target = (double(topp) + 1e-6) * Z;
-#pragma unroll
-    for (int k = 0; k < per; ++k) {
-      const int b = tid * per + k;
-      const bool before = runm > target;
-      runm += double(cnt[k]) * double(expf(-(float(b) + 1.0f) * wb - 1e-4f));
-      runc += cnt[k];
-      if (!before && runm > target) {  // one thread at most
-        m->w_bin = b;
-        m->w_n = runc;
-      }
+    if (im > target && im - lm <= target) {  // one thread at most
+      m->w_bin = tid;
+      m->i_red[kWarps - 1] = ic;
     }
+    if (tid == kThreads - 1) m->w_tot = ic;  // values counted in the window
     __syncthreads();
     jb = m->w_bin;
-    nw = m->w_n;
+    nb = (jb != INT_MAX) ? m->i_red[kWarps - 1] : 0;
+    const int tot = m->w_tot;
     __syncthreads();
     if (jb != INT_MAX || D >= kWideMaxNats) break;
+    if (tot > kWideCap) return false;  // any prefix that reaches the target is larger still
     D = fminf(2.0f * D, kWideMaxNats);  // the window held too little mass: wider
   }
-  if (jb == INT_MAX || nw > kWideCap || nw == 0) return false;
-  if (tid == 0) m->w_n = 0;
-  __syncthreads();
-  // B: collect the prefix (the bin counts are dead)
-  warp_pass(
-      c, seq, 0, policy, c.rep, c.pres, c.freq,
-      [&](float x, int col) {
-        if (x > -INFINITY && wide_bin(x, M, r, S) <= jb) {
-          const float y = __fdiv_rn(x, c.Tabs) + 0.0f;  // -0 and +0 tie
-          const int i = atomicAdd(&m->w_n, 1);
-          if (i < kWideCap) keys[i] = (uint64_t(f2key(y)) << 32) | uint64_t(~uint32_t(c.c0 + col));
-        }
-      },
-      [&](int) {}, wide_floor(M, float(jb + 1) / S, c.Tabs));
-  __syncthreads();
-  if (m->flags & F_TIMEOUT) {
-    if (tid == 0) a.out_ids[c.row] = NS_ERR_DEVICE_TIMEOUT;
-    return true;
+  if (jb == INT_MAX || nb > kWideCap || nb == 0) return false;
+  if (jb >= kb || n > kWideCap) {  // the prefix lies past the keys' bins, or they overflowed
+    if (tid == 0) m->w_n = 0;
+    __syncthreads();
+    warp_pass(
+        c, seq, 0, policy, c.rep, c.pres, c.freq,
+        [&](float x, int col) {
+          if (x > -INFINITY && wide_bin(x, M, r, S) <= jb) {
+            const int i = atomicAdd(&m->w_n, 1);
+            if (i < kWideCap) keys[i] = key_of(x, col);
+          }
+        },
+        [&](int) {}, wide_floor(M, float(jb + 1) / S, c.Tabs));
+    __syncthreads();
+    if (m->flags & F_TIMEOUT) {
+      if (tid == 0) a.out_ids[c.row] = NS_ERR_DEVICE_TIMEOUT;
+      return true;
+    }
+    n = m->w_n;
+    if (n > kWideCap || n == 0) return false;
   }
-  const int n = m->w_n;
-  if (n > kWideCap || n == 0) return false;
-  int n2 = 1;
-  while (n2 < n) n2 <<= 1;
-  for (int i = n + tid; i < n2; i += kThreads) keys[i] = 0ull;
-  __syncthreads();
-  bitonic_sort_u64(keys, n2, true);
+  uint64_t* tmp = reinterpret_cast<uint64_t*>(c.stages + size_t(kMergeCap) * 8);
+  uint64_t* sorted = reinterpret_cast<uint64_t*>(c.stages + kRankKeysOff) + kRankMax;
+  const float Sb = float(kBins - 1) / D;  // sort buckets: a function of y alone, so ties share one
+  bucket_sort(
+      m, keys, n, tmp, sorted,
+      [&](uint64_t k) {
+        const float d = (M - key2f(uint32_t(k >> 32))) * Sb;
+        return d < float(kBins - 1) ? int(fmaxf(d, 0.0f)) : kBins - 1;
+      },
+      [](uint64_t x, uint64_t y) { return x > y; });
   // exact mass of the keys above the smallest scaled value
   {
-    const uint32_t ylast = uint32_t(keys[n - 1] >> 32);
+    const uint32_t ylast = uint32_t(sorted[n - 1] >> 32);
     double cm = 0.0;
     for (int i = tid; i < n; i += kThreads) {
-      const uint32_t yk = uint32_t(keys[i] >> 32);
+      const uint32_t yk = uint32_t(sorted[i] >> 32);
       if (yk > ylast) cm += double(expf(__fsub_rn(key2f(yk), M)));
     }
 #pragma unroll
@@ -2583,10 +2634,10 @@ __device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t poli
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) tot += m->d_red[w];
     __syncthreads();
-    if (!(tot > (double(topp) + 1e-6) * Z) || key2f(uint32_t(keys[0] >> 32)) != M) return false;
+    if (!(tot > (double(topp) + 1e-6) * Z) || key2f(uint32_t(sorted[0] >> 32)) != M) return false;
   }
   c.K = n;  // no top-k: every key is a survivor
-  finalize_keys(c, a, c.row, topp, keys, n, n, Z);
+  finalize_keys(c, a, c.row, topp, sorted, n, n, Z);
   return true;
 }
 
