@@ -21,13 +21,15 @@
 //       draw run on them.  The vocabulary is never sorted.
 //   SOFTMAX (top-k and top-p both off -- the reference's defaults)
 //       one pass of per-tile maxima and float64 masses; the draw is located by
-//       warp, then tile, and one 4 KB tile is read again.
-//   NUCLEUS (top-k off, top-p on)
+//       CTA (clusters exchange maxima and masses), warp, then tile, and one
+//       4 KB tile is read again.
+//   NUCLEUS (top-k off, top-p on; one CTA per row)
 //       FAST with the kNucleusK largest as candidates plus the SOFTMAX masses;
 //       when the candidates hold more than p of the row's mass, the top-p cut
-//       and the draw run on them; otherwise the row continues on GENERAL.
+//       and the draw run on them; otherwise one more pass collects a window of
+//       values below the row's maximum (nucleus_wide), else GENERAL.
 //   GENERAL (top-k > kFastK, ties overflowing a buffer, NUCLEUS rows whose
-//       nucleus is larger, and rows of clusters with top-k off)
+//       nucleus is larger, and rows of clusters with top-k off and top-p on)
 //       a cluster-cooperative multi-pass radix search over counts and
 //       fixed-point masses; the last pass rescans one tile in id order.
 //
@@ -144,6 +146,9 @@ struct Misc {
   uint32_t pub[kWarps];     // FAST: per-warp published bound (key; 0 = none)
   double s_rem;             // SOFTMAX: the draw's remaining mass inside the chosen warp
   int s_warp;               // ... and that warp
+  int s_rank;               // ... and that CTA of the cluster
+  float c_M;                // SOFTMAX clusters: this CTA's largest scaled value
+  double c_W;               // ... and its mass with the row's largest
   float nuc_M;              // NUCLEUS: the row's largest scaled value
   double nuc_Z;             // ... and its total mass sum exp(y - nuc_M)
   float nuc_yk;             // ... and its kNucleusK-th largest scaled value (-inf: unknown)
@@ -1783,7 +1788,8 @@ __device__ __forceinline__ void write_greedy(const KArgs& a, int64_t row, int st
 // the CTAs' lists through distributed shared memory.
 // Returns false (the same on every thread of the cluster) when the row
 // continues on the general merge below: tied values that overflowed a buffer
-// (multi-pass path), or a union of more than kRankMax survivors.
+// (multi-pass path), or a union of more than kRankMax survivors in one CTA
+// (kMergeStage over a cluster's lists).
 template <int DT>
 __device__ bool row_tail(const Ctx<DT>& c, const KArgs& a, cg::cluster_group& cluster, int CL, int rank, int mode,
                          bool ok, const WarpCand& s, float best, int bidx, float topp) {
@@ -1957,7 +1963,9 @@ __device__ bool row_tail(const Ctx<DT>& c, const KArgs& a, cg::cluster_group& cl
     n_all += rm->n_merge;
   }
   const bool hard = (fl_all & (F_NAN | F_TIMEOUT | F_BADID | F_HIST)) != 0;
-  if (!hard && ((fl_all & F_OVF) || n_all > kRankMax)) {  // the multi-pass path, uniformly
+  // the lists are staged whole (kMergeStage keys) and the first kRankMax
+  // positions of their union placed; a tie run past them overflows
+  if (!hard && ((fl_all & F_OVF) || n_all > kMergeStage)) {  // the multi-pass path, uniformly
     cluster.sync();
     if (tid == 0) atomicOr(&m->flags, F_OVF);
     __syncthreads();
@@ -1983,6 +1991,28 @@ __device__ bool row_tail(const Ctx<DT>& c, const KArgs& a, cg::cluster_group& cl
     }
   }
   cluster.sync();  // the leader's reads are done before any CTA exits
+  if (!hard && n_all > kRankMax) {
+    // The same decision on every CTA: the leader places the first kRankMax
+    // positions and checks that the tie run at the k-th ends inside them;
+    // if not, the whole cluster takes the multi-pass path.
+    if (rank == 0) {
+      place_sorted_lists(lists, m->roff, CL, total, gsorted);
+      if (warp == 0) {  // warp-synchronous
+        const int nf = topk_with_ties(gsorted, kRankMax, c.K);
+        if (lane == 0) m->n_merge = (nf >= kRankMax) ? -1 : nf;
+      }
+    }
+    cluster.sync();
+    const bool over = cluster.map_shared_rank(m, 0)->n_merge < 0;
+    cluster.sync();  // the leader's verdict is read before any CTA moves on
+    if (over) {
+      if (tid == 0) atomicOr(&m->flags, F_OVF);
+      __syncthreads();
+      return false;
+    }
+    if (rank == 0) finalize_keys(c, a, row, topp, gsorted, kRankMax, total);
+    return true;
+  }
   if (rank != 0) return true;
   if (hard) {
     if (tid == 0) a.out_ids[row] = status_from_flags(fl_all, false);
@@ -2037,14 +2067,17 @@ __device__ __forceinline__ double warp_row_mass(const Ctx<DT>& c, float M) {
   return W;
 }
 
-// SOFTMAX rows on one CTA: after the stream (tile masses in place, penalised
-// history values computed), locate the draw u * Z in column order -- warp,
-// then tile -- and read that tile again to find the id.  Weights are
-// expf(rn(x / |T|) - ym_t) * expf(ym_t - M) for the tiles' values and
-// expf(rn(xp / |T|) - M) for history columns (penalised xp), summed in float64
-// in the same way for the totals and for the final scan.
+// SOFTMAX rows: after the stream (tile masses in place, penalised history
+// values computed), locate the draw u * Z in column order -- CTA of the
+// cluster, warp, then tile -- and read that tile again to find the id.
+// Weights are expf(rn(x / |T|) - ym_t) * expf(ym_t - M) for the tiles' values
+// and expf(rn(xp / |T|) - M) for history columns (penalised xp), summed in
+// float64 in the same way for the totals and for the final scan.  A cluster
+// exchanges each CTA's largest value and mass through distributed shared
+// memory (three cluster barriers on every path).
 template <int DT>
-__device__ void softmax_tail(const Ctx<DT>& c, const KArgs& a, uint64_t policy) {
+__device__ void softmax_tail(const Ctx<DT>& c, const KArgs& a, uint64_t policy, cg::cluster_group& cluster, int CL,
+                             int rank) {
   using E = Elem<DT>;
   using R = typename E::raw;
   constexpr int TE = Ctx<DT>::TE;
@@ -2060,12 +2093,25 @@ __device__ void softmax_tail(const Ctx<DT>& c, const KArgs& a, uint64_t policy) 
   const float ymax = warp_row_max(c);
   if (lane == 0) m->wbest[warp] = ymax;
   __syncthreads();
-  const int st = status_from_flags(m->flags, false);
   float M = -INFINITY;
 #pragma unroll
   for (int w = 0; w < kWarps; ++w) M = fmaxf(M, m->wbest[w]);
-  if (st != NS_OK || !(M > -INFINITY)) {
-    if (tid == 0) a.out_ids[row] = (st != NS_OK) ? st : NS_ERR_INVALID_DISTRIBUTION;
+  int fl = m->flags;
+  if (CL > 1) {
+    if (tid == 0) m->c_M = M;
+    cluster.sync();
+    M = -INFINITY;
+    fl = 0;
+    for (int r = 0; r < CL; ++r) {
+      const Misc* rm = cluster.map_shared_rank(m, r);
+      M = fmaxf(M, rm->c_M);
+      fl |= rm->flags;
+    }
+  }
+  const int st = status_from_flags(fl, false);
+  if (st != NS_OK || !(M > -INFINITY)) {  // the same decision on every CTA
+    if (CL > 1) cluster.sync();           // every CTA has read the others
+    if (rank == 0 && tid == 0) a.out_ids[row] = (st != NS_OK) ? st : NS_ERR_INVALID_DISTRIBUTION;
     return;
   }
   auto tile_scale = [&](int t) {
@@ -2073,18 +2119,41 @@ __device__ void softmax_tail(const Ctx<DT>& c, const KArgs& a, uint64_t policy) 
     return y > -INFINITY ? double(expf(__fsub_rn(y, M))) : 0.0;
   };
 
-  // 2. this warp's mass
+  // 2. this warp's mass, and this CTA's
   const double W = warp_row_mass(c, M);
   if (lane == 0) m->d_red[warp] = W;
   __syncthreads();
+  if (tid == 0) {
+    double Wc = 0.0;
+    for (int w = 0; w < kWarps; ++w) Wc += m->d_red[w];
+    m->c_W = Wc;
+  }
+  if (CL > 1)
+    cluster.sync();
+  else
+    __syncthreads();
 
-  // 3. the warp holding u * Z (the last warp with mass if rounding leaves the
-  // target past the end)
+  // 3. the CTA, then the warp holding u * Z (the last with mass if rounding
+  // leaves the target past the end); every CTA computes the same choice
   if (tid == 0) {
     const float u = a.uniforms ? c.u_pre : philox_uniform(a.seed, a.offset, uint64_t(row));
     double Z = 0.0;
-    for (int w = 0; w < kWarps; ++w) Z += m->d_red[w];
-    const double target = double(u) * Z;
+    for (int r = 0; r < CL; ++r) Z += cluster.map_shared_rank(m, r)->c_W;
+    double target = double(u) * Z;
+    int rs = -1, rlast = 0;
+    double rbefore = 0.0;
+    for (int r = 0; r < CL; ++r) {
+      const double Wr = cluster.map_shared_rank(m, r)->c_W;
+      if (Wr > 0.0) rlast = r;
+      if (rs < 0 && rbefore + Wr > target) rs = r;
+      if (rs < 0) rbefore += Wr;
+    }
+    if (rs < 0) {
+      rs = rlast;
+      rbefore = Z - cluster.map_shared_rank(m, rlast)->c_W;
+    }
+    m->s_rank = rs;
+    target -= rbefore;  // inside CTA rs
     double before = 0.0;
     int sw = -1, last = 0;
     for (int w = 0; w < kWarps; ++w) {
@@ -2099,8 +2168,9 @@ __device__ void softmax_tail(const Ctx<DT>& c, const KArgs& a, uint64_t policy) 
     m->s_warp = sw;
     m->s_rem = target - before;
   }
+  if (CL > 1) cluster.sync();  // every CTA has read the others
   __syncthreads();
-  if (warp != m->s_warp) return;
+  if (rank != m->s_rank || warp != m->s_warp) return;
 
   // 4. the tile: per-tile totals (scaled tile mass + its history columns),
   // scanned in column order 32 tiles at a time
@@ -3092,8 +3162,10 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     mode = MODE_GREEDY;
   else if (topk > 0 && int64_t(topk) < a.vocab_total && topk <= kFastK)
     mode = MODE_FAST;
-  else if (!(topk > 0 && int64_t(topk) < a.vocab_total) && CL == 1 && !a.vp_keys)
-    mode = (topp > 0.0f && topp < 1.0f) ? MODE_NUCLEUS : MODE_SOFTMAX;
+  else if (!(topk > 0 && int64_t(topk) < a.vocab_total) && !a.vp_keys && !(topp > 0.0f && topp < 1.0f))
+    mode = MODE_SOFTMAX;
+  else if (!(topk > 0 && int64_t(topk) < a.vocab_total) && !a.vp_keys && CL == 1)
+    mode = MODE_NUCLEUS;
   else
     mode = MODE_GENERAL;
   // NUCLEUS (top-k off, top-p on): the FAST filter keeps the kNucleusK largest
@@ -3327,8 +3399,8 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     }
   }
   if (fastlike && s.ovf && lane == 0) atomicOr(&m->flags, F_OVF);
-  if (mode == MODE_SOFTMAX) {  // single-CTA rows only
-    softmax_tail(c, a, policy);
+  if (mode == MODE_SOFTMAX) {
+    softmax_tail(c, a, policy, cluster, CL, rank);
     return;
   }
   int seq_next = c.wtiles(warp);  // copies this warp has made

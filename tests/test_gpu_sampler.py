@@ -187,12 +187,13 @@ def test_tie_plateau_merge_paths(sampler, n_ties, K, B):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("B", [96, 160])
+@pytest.mark.parametrize("B", [8, 96, 160])
 def test_softmax_rows_top_k_and_top_p_off(sampler, dtype, B):
     """The reference's default request (top_k -1, top_p 1.0): the draw is over
-    the whole softmax.  160 full-size rows (more than the SMs) run one block
-    per row -- the one-pass softmax path; 96 rows run 2-block clusters -- the
-    multi-pass path.  k 0 or >= V and p 0.0 also disable the filters."""
+    the whole softmax, in one pass.  160 full-size rows (more than the SMs) run
+    one block per row; 96 rows run 2-block clusters and 8 rows 8-block
+    clusters, which exchange their maxima and masses.  k 0 or >= V and p 0.0
+    also disable the filters."""
     V = 151936
     x = make_logits(61, B, V, 3.0, spike_frac=0.005, dtype=dtype)
     hs = make_histories(62, B, V, 256)
@@ -212,6 +213,26 @@ def test_softmax_rows_top_k_and_top_p_off(sampler, dtype, B):
     ids, ref = run(sampler, x_in, hs, params, u)
     assert check(ids, ref, f"softmax {dtype}") <= 3
     assert ids[3] < 0 and (dtype != torch.float32 or ids[5] < 0)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_cluster_union_past_1024_keys(sampler, dtype):
+    """Eight rows run 8-block clusters; with k up to 240 each block keeps its
+    own top-k with ties, so the leader's union of the eight lists exceeds 1024
+    keys: the lists are staged whole and the first 1024 positions placed.  A
+    row with a tie plateau larger than k checks the overflow rule."""
+    B, V = 8, 151936
+    x = make_logits(91, B, V, 3.0, dtype=torch.float32)
+    x[5, 1000:1400] = x[5].max() + 1.0        # 400 equal leaders, k = 240: ties past the k-th
+    x = x.to(dtype)
+    hs = make_histories(92, B, V, 300)
+    params = [SamplingParams(temperature=float(t), top_k=int(k), top_p=float(p),
+                             repetition_penalty=1.1, presence_penalty=0.3)
+              for t, k, p in [(0.7, 200, 0.9), (1.0, 240, 1.0), (0.5, 150, 0.95), (-0.8, 230, 0.8),
+                              (1.3, 240, 0.99), (0.7, 240, 1.0), (0.9, 180, 0.5), (1.1, 129, 0.9)]]
+    u = make_uniforms(93, B)
+    ids, ref = run(sampler, x, hs, params, u)
+    assert check(ids, ref, f"cluster union {dtype}") <= 2
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
