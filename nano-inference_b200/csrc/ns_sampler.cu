@@ -23,13 +23,14 @@
 //       one pass of per-tile maxima and float64 masses; the draw is located by
 //       CTA (clusters exchange maxima and masses), warp, then tile, and one
 //       4 KB tile is read again.
-//   NUCLEUS (top-k off, top-p on; one CTA per row)
+//   NUCLEUS (top-k off, top-p on)
 //       FAST with the kNucleusK largest as candidates plus the SOFTMAX masses;
 //       when the candidates hold more than p of the row's mass, the top-p cut
-//       and the draw run on them; otherwise one more pass collects a window of
-//       values below the row's maximum (nucleus_wide), else GENERAL.
+//       and the draw run on them; otherwise (one CTA per row) one more pass
+//       collects a window of values below the row's maximum (nucleus_wide),
+//       else GENERAL.
 //   GENERAL (top-k > kFastK, ties overflowing a buffer, NUCLEUS rows whose
-//       nucleus is larger, and rows of clusters with top-k off and top-p on)
+//       nucleus is larger)
 //       a cluster-cooperative multi-pass radix search over counts and
 //       fixed-point masses; the last pass rescans one tile in id order.
 //
@@ -1774,7 +1775,7 @@ __device__ __forceinline__ void write_greedy(const KArgs& a, int64_t row, int st
   }
 }
 
-// The end of a GREEDY, FAST or NUCLEUS row (NUCLEUS: one CTA only) with few
+// The end of a GREEDY, FAST or NUCLEUS row with few
 // barriers.
 // GREEDY: each CTA reduces its warps' (value, first index); a cluster's
 // leader reads the CTAs' results in parallel.
@@ -1955,6 +1956,12 @@ __device__ bool row_tail(const Ctx<DT>& c, const KArgs& a, cg::cluster_group& cl
     const int nf = topk_with_ties(sorted, min(n, kRankMax), c.K);
     if (lane == 0) m->n_merge = nf;
   }
+  if (nuc && tid == 0) {  // this CTA's largest scaled value and its mass below it
+    double Wc = 0.0;
+    for (int w = 0; w < kWarps; ++w) Wc += m->d_red[w];
+    m->c_M = M;
+    m->c_W = Wc;
+  }
   cluster.sync();
   int fl_all = 0, n_all = 0;
   for (int r = 0; r < CL; ++r) {
@@ -1991,15 +1998,35 @@ __device__ bool row_tail(const Ctx<DT>& c, const KArgs& a, cg::cluster_group& cl
     }
   }
   cluster.sync();  // the leader's reads are done before any CTA exits
-  if (!hard && n_all > kRankMax) {
+  if (!hard && (n_all > kRankMax || nuc)) {
     // The same decision on every CTA: the leader places the first kRankMax
-    // positions and checks that the tie run at the k-th ends inside them;
-    // if not, the whole cluster takes the multi-pass path.
+    // positions and checks that the tie run at the k-th ends inside them
+    // (NUCLEUS: and that the candidates hold more than p of the row's mass,
+    // rebuilt from the CTAs' maxima and masses); if not, the whole cluster
+    // takes the multi-pass path.
+    const int np = min(n_all, kRankMax);
     if (rank == 0) {
       place_sorted_lists(lists, m->roff, CL, total, gsorted);
       if (warp == 0) {  // warp-synchronous
-        const int nf = topk_with_ties(gsorted, kRankMax, c.K);
-        if (lane == 0) m->n_merge = (nf >= kRankMax) ? -1 : nf;
+        const int nf = topk_with_ties(gsorted, np, c.K);
+        bool good = !(nf >= np && n_all > np);
+        if (nuc) {
+          float Mg = -INFINITY;
+          for (int r = 0; r < CL; ++r) Mg = fmaxf(Mg, cluster.map_shared_rank(m, r)->c_M);
+          double Z = 0.0;
+          for (int r = 0; r < CL; ++r) {
+            const Misc* rm = cluster.map_shared_rank(m, r);
+            if (rm->c_M > -INFINITY) Z += rm->c_W * double(expf(__fsub_rn(rm->c_M, Mg)));
+          }
+          double cm = 0.0;
+          for (int j = lane; j < nf; j += 32) cm += double(expf(__fsub_rn(key2f(uint32_t(gsorted[j] >> 32)), Mg)));
+#pragma unroll
+          for (int o = 16; o; o >>= 1) cm += __shfl_xor_sync(kFull, cm, o);
+          good = good && nf > 0 && Mg > -INFINITY && key2f(uint32_t(gsorted[0] >> 32)) == Mg &&
+                 cm > (double(topp) + 1e-6) * Z;
+          if (lane == 0) m->nuc_Z = Z;
+        }
+        if (lane == 0) m->n_merge = good ? nf : -1;
       }
     }
     cluster.sync();
@@ -2010,7 +2037,7 @@ __device__ bool row_tail(const Ctx<DT>& c, const KArgs& a, cg::cluster_group& cl
       __syncthreads();
       return false;
     }
-    if (rank == 0) finalize_keys(c, a, row, topp, gsorted, kRankMax, total);
+    if (rank == 0) finalize_keys(c, a, row, topp, gsorted, np, n_all, nuc ? m->nuc_Z : -1.0);
     return true;
   }
   if (rank != 0) return true;
@@ -3164,7 +3191,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     mode = MODE_FAST;
   else if (!(topk > 0 && int64_t(topk) < a.vocab_total) && !a.vp_keys && !(topp > 0.0f && topp < 1.0f))
     mode = MODE_SOFTMAX;
-  else if (!(topk > 0 && int64_t(topk) < a.vocab_total) && !a.vp_keys && CL == 1)
+  else if (!(topk > 0 && int64_t(topk) < a.vocab_total) && !a.vp_keys)
     mode = MODE_NUCLEUS;
   else
     mode = MODE_GENERAL;
@@ -3407,7 +3434,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
   if (mode != MODE_GENERAL) {
     if (row_tail(c, a, cluster, CL, rank, mode, ok, s, best, bidx, topp)) return;
     __syncthreads();  // the row continues below
-    if (mode == MODE_NUCLEUS && nucleus_wide(c, a, seq_next, policy, topp)) return;  // one CTA
+    if (mode == MODE_NUCLEUS && CL == 1 && nucleus_wide(c, a, seq_next, policy, topp)) return;
   }
   if (fastlike) {  // every warp's final bound; survivors of the tightest
     if (ok) publish_bound(c, s);

@@ -236,13 +236,15 @@ def test_cluster_union_past_1024_keys(sampler, dtype):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("B", [96, 160])
+@pytest.mark.parametrize("B", [12, 96, 160])
 def test_nucleus_rows_top_k_off(sampler, dtype, B):
-    """Top-k off with top-p on.  One block per row (160 rows): the stream keeps
-    the 128 largest as candidates and checks they hold more than p of the
-    row's mass; larger nuclei take two more passes (a plateau of 300 near-equal
-    leaders), and a nucleus past the key capacity (a flat row) the multi-pass
-    path.  Clusters (96 rows) take the multi-pass path."""
+    """Top-k off with top-p on.  The stream keeps the 128 largest as
+    candidates and checks they hold more than p of the row's mass.  One block
+    per row (160 rows): larger nuclei take one more pass (a plateau of 300
+    near-equal leaders), and a nucleus past the key capacity (a flat row) the
+    multi-pass path.  Clusters (96 rows: 2 blocks, 12 rows: 8 blocks) check the
+    merged candidates against the mass rebuilt from every block, and take the
+    multi-pass path when they fall short."""
     V = 151936
     x = make_logits(71, B, V, 3.0, spike_frac=0.005, dtype=torch.float32)
     x[7] = torch.randn(V, generator=torch.Generator().manual_seed(7)) * 0.01    # nucleus ~ 0.9 V
