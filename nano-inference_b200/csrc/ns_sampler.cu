@@ -704,16 +704,21 @@ __device__ __forceinline__ void load_full(const uint8_t* st, uint4 (&v)[kGroupsP
 // tau (or is NaN) and one vote; hot groups are re-read from shared memory one
 // per lane per round (lanes may work on different groups in one round).
 template <int DT, bool NEG>
-__device__ __forceinline__ void fast_full(const Ctx<DT>& c, WarpCand& s, const uint8_t* st, int colbase) {
-  constexpr int VE = Ctx<DT>::VE, TE = Ctx<DT>::TE, G = kGroupsPerLane<DT>;
-  const int lane = threadIdx.x & 31;
+__device__ __forceinline__ unsigned full_hot_mask(const WarpCand& s, const uint8_t* st) {
+  constexpr int G = kGroupsPerLane<DT>;
   unsigned gm = 0;
-  {
-    uint4 v[G];
-    load_full<DT>(st, v);
+  uint4 v[G];
+  load_full<DT>(st, v);
 #pragma unroll
-    for (int k = 0; k < G; ++k) gm |= (group_extreme<DT, NEG>(v[k]) < s.tau ? 0u : 1u) << k;
-  }
+  for (int k = 0; k < G; ++k) gm |= (group_extreme<DT, NEG>(v[k]) < s.tau ? 0u : 1u) << k;
+  return gm;
+}
+
+template <int DT, bool NEG>
+__device__ __forceinline__ void fast_full(const Ctx<DT>& c, WarpCand& s, const uint8_t* st, int colbase,
+                                          unsigned gm) {
+  constexpr int VE = Ctx<DT>::VE, TE = Ctx<DT>::TE;
+  const int lane = threadIdx.x & 31;
   while (__any_sync(kFull, gm != 0u)) {
     const bool h = gm != 0u;
     const int k = h ? __ffs(gm) - 1 : 0;
@@ -728,6 +733,29 @@ __device__ __forceinline__ void fast_full(const Ctx<DT>& c, WarpCand& s, const u
     }
     const bool hh = h && !cold;
     if (__any_sync(kFull, hh)) group_append(c, s, k * 32 + lane, x, hh, 0, TE, TE / VE, colbase);
+  }
+}
+
+// GREEDY of a full tile already in registers (gx: the groups' maxima).
+template <int DT>
+__device__ __forceinline__ void greedy_regs(const uint4 (&v)[kGroupsPerLane<DT>],
+                                            const float (&gx)[kGroupsPerLane<DT>], int colbase, float& best,
+                                            int& bidx) {
+  constexpr int VE = Ctx<DT>::VE, G = kGroupsPerLane<DT>;
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < G; ++k) {
+    if (gx[k] <= best && bidx != INT_MAX) continue;
+    float x[VE];
+    unpack16<DT>(v[k], x);
+#pragma unroll
+    for (int i = 0; i < VE; ++i) {
+      const int col = colbase + (k * 32 + lane) * VE + i;
+      if (better(x[i], col, best, bidx)) {
+        best = x[i];
+        bidx = col;
+      }
+    }
   }
 }
 
@@ -766,7 +794,7 @@ __device__ __forceinline__ void fast_tile(const Ctx<DT>& c, WarpCand& s, int w, 
   const int n_groups = (lead + len + VE - 1) / VE;
   const int colbase = w * c.pw + t * TE - lead;  // CTA-relative column of slot 0
   if (full) {
-    fast_full<DT, NEG>(c, s, st, colbase);
+    fast_full<DT, NEG>(c, s, st, colbase, full_hot_mask<DT, NEG>(s, st));
     return;
   }
   for (int q0 = 0; q0 < n_groups; q0 += 64) {
@@ -1081,6 +1109,47 @@ __device__ __forceinline__ bool stream_warp_t(const Ctx<DT>& c, uint64_t policy,
       if (c.pen) {
         mask_tile(c, w, t, st);
         __syncwarp();
+      }
+    }
+    // Full tiles: the stage is refilled as soon as its bytes are no longer
+    // needed -- GREEDY once the tile is in registers, FAST once no group of
+    // it reaches tau (every load has been waited for by then).
+    auto issue_next = [&]() {
+      if (lane == 0 && t + kWStages < nt) {
+        const int tn = t + kWStages;
+        if (tn < nfull)
+          issue_full_tile(c, w, tn, tn % kWStages, policy);
+        else
+          issue_tile(c, w, tn, tn % kWStages, policy);
+      }
+    };
+    if constexpr (MODE == MODE_GREEDY) {
+      if (t < nfull) {
+        constexpr int G = kGroupsPerLane<DT>;
+        uint4 v[G];
+        float gx[G];
+        load_full<DT>(st, v);
+#pragma unroll
+        for (int k = 0; k < G; ++k) gx[k] = group_extreme<DT, false>(v[k]);
+        __syncwarp();
+        issue_next();
+        greedy_regs<DT>(v, gx, c.c0 + w * c.pw + t * Ctx<DT>::TE, best, bidx);  // full tiles: lead 0
+        continue;
+      }
+    }
+    if constexpr (MODE == MODE_FAST) {
+      if (t < nfull && !s.ovf) {
+        const unsigned gm = full_hot_mask<DT, NEG>(s, st);
+        const bool hot = __any_sync(kFull, gm != 0u);
+        if (!hot) issue_next();
+        else fast_full<DT, NEG>(c, s, st, w * c.pw + t * Ctx<DT>::TE, gm);
+        if (t == 1 || t == 4 || t == 9) publish_bound(c, s);
+        read_shared_tau(c, s);
+        if (hot) {
+          __syncwarp();
+          issue_next();
+        }
+        continue;
       }
     }
     if constexpr (MODE == MODE_GREEDY) {
