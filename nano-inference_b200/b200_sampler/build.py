@@ -44,6 +44,32 @@ def sources():
     return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
 
 
+HISTPACK_SRC = os.path.join(CSRC, "histpack.c")
+
+
+def histpack_path() -> str:
+    import sysconfig
+    return os.path.join(PKG_DIR, "_histpack" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_histpack(force: bool = False) -> str:
+    """Compile the host-side history packer (a CPython extension, plain C)."""
+    import sysconfig
+    out = histpack_path()
+    if not force and os.path.exists(out) and os.path.getmtime(out) >= os.path.getmtime(HISTPACK_SRC):
+        return out
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        raise RuntimeError("no C compiler for the history packer")
+    tmp = out + ".tmp"
+    cmd = [cc, "-O3", "-shared", "-fPIC", "-I", sysconfig.get_paths()["include"], "-o", tmp, HISTPACK_SRC]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("gcc failed:\n" + r.stdout + r.stderr)
+    os.replace(tmp, out)
+    return out
+
+
 def _deps():
     return sources() + glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(INCLUDE, "*.h"))
 
@@ -56,7 +82,9 @@ def needs_build() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
-    """Compile csrc/*.cu into the in-tree shared library; returns its path."""
+    """Compile csrc/*.cu into the in-tree shared library (and the history
+    packer); returns the library's path."""
+    build_histpack(force)
     if not force and not needs_build():
         return LIB_PATH
     tmp = LIB_PATH + ".tmp"

@@ -34,6 +34,11 @@ import torch
 from . import _lib
 from .params import pack_params
 
+try:  # C-level history packing (built with the library); array.array otherwise
+    from ._histpack import pack as _pack_histories
+except ImportError:  # pragma: no cover - a tree without the built packer
+    _pack_histories = None
+
 try:  # the reference's ABC when nano-inference is installed
     from nano_inference.sampling.base import SamplerBase  # type: ignore
 except Exception:  # pragma: no cover - mirror of sampling/base.py:10-25
@@ -125,6 +130,7 @@ class B200Sampler(SamplerBase):
         self.seed = int(seed) & 0xFFFFFFFFFFFFFFFF
         self.offset = 0
         self._staging = {}
+        self._landing = {}   # device index -> (device buffer for host logits, event after its last reader)
         self._lock = threading.Lock()
 
     # ------------------------------------------------------------------ API
@@ -163,17 +169,18 @@ class B200Sampler(SamplerBase):
         if logits.dtype not in _DTYPES:
             raise TypeError(f"unsupported logits dtype {logits.dtype}")
         device = self._device_for(logits)
-        if logits.device != device:
-            logits = logits.to(device, non_blocking=True)
-        if logits.stride(1) != 1:
-            logits = logits.contiguous()
         stream = torch.cuda.current_stream(device)
+        if logits.device == device and logits.stride(1) != 1:
+            logits = logits.contiguous()
         if out is None:
             out = torch.empty(B, dtype=torch.int64, device=device)
         if B == 0:
             return out
 
         with self._lock:
+            landed = None
+            if logits.device != device:
+                logits, landed = self._land(logits, device, stream)
             st = self._stage(device, B, all_generated_ids, all_sampling_params, uniforms, stream)
             offset = self.offset
             self.offset += 1
@@ -185,6 +192,8 @@ class B200Sampler(SamplerBase):
                 st.u_ptr, self.seed, offset,
                 out.data_ptr(), None, 0, stream.cuda_stream)
             st.keep_alive(stream)
+            if landed is not None:
+                landed.record(stream)   # the next call's copy waits for this launch
         if rc != _lib.NS_OK:
             raise RuntimeError(f"ns_sample failed: {_lib.status_string(rc)}")
         return out
@@ -219,13 +228,16 @@ class B200Sampler(SamplerBase):
             offs[0] = 0
             np.cumsum(lens, out=offs[1:])
             ids32 = h[off_ids:off_ids + total * 4].view(np.int32)
-            pos = 0
-            try:  # one C-level conversion per row (ids beyond int32 cannot be token ids)
-                for row in all_generated_ids:
-                    n = len(row)
-                    if n:
-                        ids32[pos:pos + n] = np.frombuffer(array.array("i", row), dtype=np.int32)
-                        pos += n
+            try:  # ids beyond int32 cannot be token ids
+                if _pack_histories is not None:
+                    _pack_histories(all_generated_ids, ids32)
+                else:
+                    pos = 0
+                    for row in all_generated_ids:
+                        n = len(row)
+                        if n:
+                            ids32[pos:pos + n] = np.frombuffer(array.array("i", row), dtype=np.int32)
+                            pos += n
             except OverflowError:
                 raise IndexError(_lib.status_string(_lib.NS_ERR_TOKEN_ID_OUT_OF_RANGE)) from None
         if host_u:
@@ -252,6 +264,26 @@ class B200Sampler(SamplerBase):
                        max_hist=max_hist, u_ptr=u_ptr, u_dev=ud)
 
     # -------------------------------------------------------------- helpers
+    def _land(self, logits: torch.Tensor, device: torch.device, stream: torch.cuda.Stream):
+        """Copy host (or other-device) logits into a per-device buffer that is
+        kept between calls: a fresh allocation per call roughly quarters the
+        pinned host-to-device rate.  Returns the device view and the event to
+        record after the launch that reads it.  Call under the lock."""
+        buf, ev = self._landing.get(device.index, (None, None))
+        need = logits.numel()
+        if buf is None or buf.numel() < need or buf.dtype != logits.dtype:
+            if ev is not None:
+                ev.synchronize()
+            buf = torch.empty(max(need, 1), dtype=logits.dtype, device=device)
+            ev = torch.cuda.Event()
+            self._landing[device.index] = (buf, ev)
+        else:
+            stream.wait_event(ev)   # the previous reader of the buffer is done
+        dst = buf[:need].view(logits.shape)
+        with torch.cuda.stream(stream):
+            dst.copy_(logits, non_blocking=True)
+        return dst, ev
+
     def _device_for(self, logits: torch.Tensor) -> torch.device:
         if logits.is_cuda:
             return logits.device
