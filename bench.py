@@ -342,13 +342,15 @@ def run_ours(args, world, rank, local):
 def run_vp(args, world, rank, local):
     """vocab-parallel sampling, B=128 rows of V=151936 fp32
     split into `world` contiguous slices; per step ns_vp_local on this rank's
-    slice, an all-gather of the candidate records (NCCL), ns_vp_merge.  Total
-    work is fixed as N grows (strong scaling); tokens/s counts the B rows once."""
+    slice, then the exchange of the candidate records -- `peer`: ns_vp_signal
+    and ns_vp_merge_peers, which reads every rank's record in place over
+    NVLink; `gather`: an NCCL all-gather and ns_vp_merge.  Total work is fixed
+    as N grows (strong scaling); tokens/s counts the B rows once."""
     import ctypes
     import torch.distributed as dist
     from b200_sampler import _lib
     from b200_sampler.params import SamplingParams, pack_params
-    from b200_sampler.vocab_parallel import gather_records
+    from b200_sampler.vocab_parallel import PeerExchange, _ptr_array, gather_records
     from b200_sampler.workloads import make_logits, make_uniforms
 
     dev = torch.device("cuda", local)
@@ -371,25 +373,42 @@ def run_vp(args, world, rank, local):
     rec = torch.empty(n.value, dtype=torch.int64, device=dev)
     out = torch.empty(B, dtype=torch.int64, device=dev)
     side = torch.cuda.Stream(dev)
+    peer = args.vp_transport == "peer"
+    if peer:
+        ex = PeerExchange(lib, None, world, rank, dev)
+        ex.ensure(int(n.value), side)
+        flags_arg, _k1 = _ptr_array([ex.flags(r) for r in range(world)])
+        recs_arg = [_ptr_array([ex.record(r, par) for r in range(world)]) for par in (0, 1)]
 
     def step(i):
+        # step i writes record buffer i % 2: every run of steps alternates
         x = bufs[i % N_BUFFERS]
+        rp = ex.record(rank, i & 1) if peer else rec.data_ptr()
         rc = lib.ns_vp_local(x.data_ptr(), _lib.NS_DTYPE_F32, B, width, width, off, V, None, None, 0,
-                             pp, pp + 4 * B, pp + 8 * B, None, None, None, cap, rec.data_ptr(), side.cuda_stream)
+                             pp, pp + 4 * B, pp + 8 * B, None, None, None, cap, rp, side.cuda_stream)
         assert rc == 0
-        g = gather_records(rec) if world > 1 else rec
-        rc = lib.ns_vp_merge(g.data_ptr(), world, B, cap, V, pp, pp + 4 * B, pp + 8 * B, u.data_ptr(), 0, 0,
-                             out.data_ptr(), side.cuda_stream)
+        if peer:
+            rc = lib.ns_vp_signal(flags_arg, world, rank, ex.counter(), side.cuda_stream)
+            assert rc == 0
+            rc = lib.ns_vp_merge_peers(recs_arg[i & 1][0], world, ex.flags(rank), ex.counter(), B, cap, V,
+                                       pp, pp + 4 * B, pp + 8 * B, u.data_ptr(), 0, 0,
+                                       out.data_ptr(), side.cuda_stream)
+        else:
+            g = gather_records(rec) if world > 1 else rec
+            rc = lib.ns_vp_merge(g.data_ptr(), world, B, cap, V, pp, pp + 4 * B, pp + 8 * B, u.data_ptr(), 0, 0,
+                                 out.data_ptr(), side.cuda_stream)
         assert rc == 0
 
     with torch.cuda.stream(side):
-        for i in range(max(args.warmup, 3)):
+        for i in range(max(args.warmup, 3) + (max(args.warmup, 3) & 1)):   # even: the graphs start on buffer 0
             step(i)
     torch.cuda.synchronize(dev)
     assert int(out.min()) >= 0
 
-    # CUDA graphs of up to 100 steps (every rank captures the same collectives)
+    # CUDA graphs of up to 100 steps (every rank captures the same collectives;
+    # an even count keeps the record buffers alternating across replays)
     per = min(args.steps, 100)
+    per -= per & 1 if per > 1 else 0
     reps, rem = divmod(args.steps, per)
 
     def capture(nsteps):
@@ -418,6 +437,8 @@ def run_vp(args, world, rank, local):
         torch.cuda.synchronize(dev)
     barrier(world)
     del g, g_rem  # graphs holding NCCL calls go before the process group
+    if peer:
+        ex.release(side)
     ms = max_over_ranks(world, e0.elapsed_time(e1))
     ms_per_step = ms / args.steps
     peak, peak_kind = _peaks()
@@ -428,12 +449,14 @@ def run_vp(args, world, rank, local):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded randn*3 logits)",
             "config": {"workload": f"B={B} V={V} fp32 split into {world} slices of <= {w}; T=0.8 k={K} p=0.95",
                        "record_bytes_per_rank": int(n.value) * 8,
-                       "timing": f"CUDA graphs of local + NCCL all-gather + merge ({per} steps x {reps}"
+                       "transport": ("peer: records read in place over NVLink by the merge kernel after a "
+                                     "flag signal" if peer else "gather: NCCL all-gather of the records"),
+                       "timing": f"CUDA graphs of local + exchange + merge ({per} steps x {reps}"
                                  f"{f' + {rem}' if rem else ''}), CUDA events, max over ranks"},
             "roofline": {"bound": "hbm", "achieved": local_bytes / (ms_per_step / 1e3) / 1e9, "peak": peak,
                          "unit": "GB/s", "frac": local_bytes / (ms_per_step / 1e3) / 1e9 / peak,
                          "traffic": None, "peak_kind": peak_kind, "algorithmic_bytes_per_launch": local_bytes},
-            "gpu_launches": 2 * args.steps}
+            "gpu_launches": (3 if peer else 2) * args.steps}
     clocks = clk.summary()
     if clocks is not None:
         line["clocks"] = clocks
@@ -449,6 +472,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
+    ap.add_argument("--vp-transport", default="peer", choices=["peer", "gather"],
+                    help="vp mode: records read in place over NVLink (peer) or all-gathered (gather)")
     ap.add_argument("--mode", default="rows", choices=["rows", "vp"],
                     help="rows: the headline (rows sharded); vp: vocab-parallel config 4")
     args = ap.parse_args()

@@ -140,6 +140,41 @@ int ns_vp_merge(const int64_t* gathered, int n_ranks, int64_t batch, int cap, in
                 const float* uniforms, uint64_t philox_seed, uint64_t philox_offset,
                 int64_t* out_ids, ns_stream_t stream);
 
+/*
+ * Peer-memory exchange for the vocab-parallel merge (no reference
+ * counterpart).  Instead of an all-gather, every rank keeps its record in its
+ * own device memory and the merge kernel reads all ranks' records in place
+ * over NVLink (peer loads), after a bounded wait on flags the ranks set.
+ * Per step (two record buffers used on alternate steps, so a rank never
+ * overwrites a record a peer may still read; `epoch` is this rank's step
+ * counter in device memory, zero at first):
+ *   ns_vp_local(... record = my_records[step % 2] ...)
+ *   ns_vp_signal(rank_flags, n, me, epoch)   -- ++*epoch; every rank's flags[me] = *epoch
+ *   ns_vp_merge_peers(records[r] = rank r's my_records[step % 2], ..., my_flags, epoch)
+ * The merge waits until my_flags[r] >= *epoch for every r; a rank whose
+ * flags do not get there within 200 ms gets NS_ERR_DEVICE_TIMEOUT in its
+ * out_ids.  The counter lives on the device, so a captured CUDA graph of an
+ * even number of steps can be replayed.  n_ranks in [1, 8].
+ */
+#define NS_IPC_HANDLE_BYTES 64
+
+int ns_vp_signal(int64_t* const* rank_flags, int n_ranks, int my_rank, int64_t* epoch, ns_stream_t stream);
+
+int ns_vp_merge_peers(const int64_t* const* rank_records, int n_ranks, const int64_t* my_flags,
+                      const int64_t* epoch, int64_t batch, int cap, int64_t vocab_total, const float* temperature,
+                      const int32_t* top_k, const float* top_p, const float* uniforms, uint64_t philox_seed,
+                      uint64_t philox_offset, int64_t* out_ids, ns_stream_t stream);
+
+/* Device buffer for records and flags (zero-filled), and its release. */
+int ns_vp_peer_alloc(size_t bytes, void** out_ptr);
+int ns_vp_peer_free(void* ptr);
+
+/* CUDA IPC: a buffer's handle (NS_IPC_HANDLE_BYTES bytes, host memory) and
+ * its mapping in another process on the same node (peer access enabled). */
+int ns_ipc_handle(const void* ptr, void* out_handle);
+int ns_ipc_open(const void* handle, void** out_ptr);
+int ns_ipc_close(void* ptr);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,6 +13,7 @@ import threading
 from .build import LIB_PATH
 
 NS_OK = 0
+NS_IPC_HANDLE_BYTES = 64
 NS_ERR_INVALID_ARGUMENT = -1
 NS_ERR_WORKSPACE_TOO_SMALL = -2
 NS_ERR_UNSUPPORTED_DTYPE = -3
@@ -62,6 +63,19 @@ PROTOTYPES = {
         _c_vp, _c_u64, _c_u64,                       # uniforms, philox_seed, philox_offset
         _c_vp, _c_vp,                                # out_ids, stream
     ]),
+    "ns_vp_signal": (_c_int, [_c_vp, _c_int, _c_int, _c_vp, _c_vp]),    # rank_flags[], n, me, epoch, stream
+    "ns_vp_merge_peers": (_c_int, [
+        _c_vp, _c_int, _c_vp, _c_vp,                 # rank_records[], n_ranks, my_flags, epoch
+        _c_i64, _c_int, _c_i64,                      # batch, cap, vocab_total
+        _c_vp, _c_vp, _c_vp,                         # temperature, top_k, top_p
+        _c_vp, _c_u64, _c_u64,                       # uniforms, philox_seed, philox_offset
+        _c_vp, _c_vp,                                # out_ids, stream
+    ]),
+    "ns_vp_peer_alloc": (_c_int, [_c_sz, ctypes.POINTER(_c_vp)]),
+    "ns_vp_peer_free": (_c_int, [_c_vp]),
+    "ns_ipc_handle": (_c_int, [_c_vp, _c_vp]),
+    "ns_ipc_open": (_c_int, [_c_vp, ctypes.POINTER(_c_vp)]),
+    "ns_ipc_close": (_c_int, [_c_vp]),
 }
 
 _lock = threading.Lock()

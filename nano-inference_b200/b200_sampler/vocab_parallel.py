@@ -7,13 +7,18 @@ No reference counterpart: nano-inference samples whole rows
 1. ``ns_vp_local`` on this rank's slice: history penalties for the ids the
    slice holds, then per row the slice's top-k survivors (ties at the k-th
    scaled value kept) as 64-bit keys, or one key for greedy rows;
-2. ``gather_records``: all-gather of those fixed-size records (NCCL over
-   NVLink; a few KB per row);
-3. ``ns_vp_merge`` on every rank: the global top-k with ties, top-p and the
+2. the exchange of those fixed-size records (a few KB per row), either
+   - ``peer`` (default with NCCL, at most 8 ranks): each rank keeps its record
+     in its own device memory, mapped by every other rank (CUDA IPC);
+     ``ns_vp_signal`` sets a flag on every rank and ``ns_vp_merge_peers``
+     waits for all flags and reads every record in place over NVLink, in the
+     merge kernel itself; or
+   - ``gather``: ``gather_records``, an all-gather (NCCL or gloo);
+3. the merge on every rank: the global top-k with ties, top-p and the
    inverse-CDF draw.  The global top-k set lies inside the union of the
    slices' top-k sets, so the ids equal ``B200Sampler`` on whole rows.
 
-Rows with top-k off or k > 128 have no bounded candidate set; their slices are
+Rows with top-k off or k > 240 have no bounded candidate set; their slices are
 all-gathered into whole rows (``gather_full_rows``) and sampled with
 ``ns_sample`` on every rank.  With ``uniforms=None`` those rows draw from the
 Philox stream at their position in that sub-batch (still identical on every
@@ -21,6 +26,7 @@ rank).
 """
 from __future__ import annotations
 
+import ctypes
 from typing import List, Optional, Sequence
 
 import numpy as np
@@ -64,6 +70,81 @@ def gather_full_rows(rows: torch.Tensor, offsets: Sequence[int], widths: Sequenc
     return full
 
 
+class PeerExchange:
+    """Records and flags that every rank of a group reads in place: one device
+    buffer per rank (two records, used on alternate steps, then one int64
+    flag per rank and this rank's step counter), mapped into every other rank
+    with CUDA IPC.  Growing it is collective (every rank calls ``ensure`` with
+    the same size)."""
+
+    def __init__(self, lib, group, world: int, rank: int, device: torch.device):
+        self.lib, self.group, self.world, self.rank, self.device = lib, group, world, rank, device
+        self.rec_bytes = 0
+        self.bases: List[int] = []      # rank r's buffer as seen from this process
+        self.steps = 0                  # steps exchanged so far (the same on every rank)
+
+    def ensure(self, rec_int64s: int, stream: torch.cuda.Stream):
+        need = (rec_int64s * 8 + 255) // 256 * 256
+        if need <= self.rec_bytes:
+            return
+        self.release(stream)
+        flag_bytes = ((self.world + 1) * 8 + 255) // 256 * 256   # flags, then the step counter
+        with torch.cuda.device(self.device):
+            own = ctypes.c_void_p()
+            rc = self.lib.ns_vp_peer_alloc(2 * need + flag_bytes, ctypes.byref(own))
+            if rc != _lib.NS_OK:
+                raise RuntimeError(f"ns_vp_peer_alloc failed: {_lib.status_string(rc)}")
+            handle = ctypes.create_string_buffer(_lib.NS_IPC_HANDLE_BYTES)
+            rc = self.lib.ns_ipc_handle(own, handle)
+            if rc != _lib.NS_OK:
+                raise RuntimeError(f"ns_ipc_handle failed: {_lib.status_string(rc)}")
+            handles: List[Optional[bytes]] = [handle.raw]
+            if self.world > 1:
+                handles = [None] * self.world
+                dist.all_gather_object(handles, handle.raw, group=self.group)
+            bases = []
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    bases.append(own.value)
+                    continue
+                p = ctypes.c_void_p()
+                rc = self.lib.ns_ipc_open(ctypes.create_string_buffer(h, len(h)), ctypes.byref(p))
+                if rc != _lib.NS_OK:
+                    raise RuntimeError(f"ns_ipc_open failed (rank {r}): {_lib.status_string(rc)}")
+                bases.append(p.value)
+        self.bases, self.rec_bytes = bases, need
+
+    def release(self, stream: torch.cuda.Stream):
+        """Collective: once every rank's kernels are done with the buffers,
+        unmap the peers' and free this rank's."""
+        if not self.bases:
+            return
+        stream.synchronize()
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for r, b in enumerate(self.bases):
+                if r != self.rank:
+                    self.lib.ns_ipc_close(ctypes.c_void_p(b))
+            self.lib.ns_vp_peer_free(ctypes.c_void_p(self.bases[self.rank]))
+        self.bases, self.rec_bytes = [], 0
+
+    def record(self, r: int, parity: int) -> int:
+        return self.bases[r] + parity * self.rec_bytes
+
+    def flags(self, r: int) -> int:
+        return self.bases[r] + 2 * self.rec_bytes
+
+    def counter(self) -> int:
+        """This rank's step counter (device memory, advanced by ns_vp_signal)."""
+        return self.flags(self.rank) + 8 * self.world
+
+
+def _ptr_array(ptrs: Sequence[int]) -> ctypes.c_void_p:
+    arr = (ctypes.c_void_p * len(ptrs))(*ptrs)
+    return ctypes.cast(arr, ctypes.c_void_p), arr   # keep arr alive with the pointer
+
+
 class VocabParallelSampler(B200Sampler):
     """``SamplerBase`` over a vocab-parallel slice.
 
@@ -77,13 +158,16 @@ class VocabParallelSampler(B200Sampler):
         tie_slack: record entries beyond the batch's largest top_k for values
             tied at a slice's k-th value; a row whose slice overflows is
             retried once with the largest capacity.
+        transport: "peer" (records read in place over NVLink by the merge
+            kernel), "gather" (all-gather), or "auto": "peer" on an NCCL group
+            of at most 8 ranks, else "gather".
 
     Every rank must call with the same histories, params and uniforms (the
     engine replicates them); the logits are this rank's slice.
     """
 
     def __init__(self, vocab_total: int, vocab_offset: int, vocab_local: int, group=None, device=None,
-                 seed: Optional[int] = None, tie_slack: int = 16):
+                 seed: Optional[int] = None, tie_slack: int = 16, transport: str = "auto"):
         super().__init__(device=device, seed=seed)
         self.group = group
         self.world = dist.get_world_size(group)
@@ -105,6 +189,18 @@ class VocabParallelSampler(B200Sampler):
             pos += w
         if pos != self.vocab_total:
             raise ValueError("rank slices must cover the whole vocabulary")
+        if transport == "auto":
+            transport = "peer" if dist.get_backend(group) == "nccl" and self.world <= 8 else "gather"
+        if transport not in ("peer", "gather"):
+            raise ValueError(f"unknown transport {transport!r}")
+        self.transport = transport
+        self._exchange: Optional[PeerExchange] = None
+
+    def close(self):
+        """Collective: release the peer-exchange buffers (every rank calls it)."""
+        if self._exchange is not None:
+            self._exchange.release(torch.cuda.current_stream(self._exchange.device))
+            self._exchange = None
 
     def select_batch_tensor(self, logits: torch.Tensor, all_generated_ids, all_sampling_params, *,
                             uniforms: Optional[torch.Tensor] = None,
@@ -139,7 +235,18 @@ class VocabParallelSampler(B200Sampler):
         if cap is None:
             kmax = int(top_k[fast].max()) if fast.any() else 0
             cap = min(MAX_CAP, max(1, kmax + self.tie_slack))
-        rec = torch.empty(B * (1 + cap), dtype=torch.int64, device=device)
+        peer = self.transport == "peer"
+        if peer:
+            if self._exchange is None:
+                self._exchange = PeerExchange(self.lib, self.group, self.world, self.rank, device)
+            ex = self._exchange
+            ex.ensure(B * (1 + cap), stream)
+            ex.steps += 1
+            par = ex.steps & 1
+            rec_ptr = ex.record(self.rank, par)
+        else:
+            rec = torch.empty(B * (1 + cap), dtype=torch.int64, device=device)
+            rec_ptr = rec.data_ptr()
         with self._lock:
             st = self._stage(device, B, all_generated_ids, all_sampling_params, uniforms, stream)
             if offset is None:
@@ -150,14 +257,25 @@ class VocabParallelSampler(B200Sampler):
                 self.vocab_offset, self.vocab_total,
                 st.hist_ids, st.hist_offsets, st.max_hist,
                 st.p32, st.p32 + 4 * B, st.p32 + 8 * B, st.p32 + 12 * B, st.p32 + 16 * B, st.p32 + 20 * B,
-                cap, rec.data_ptr(), stream.cuda_stream)
+                cap, rec_ptr, stream.cuda_stream)
             if rc != _lib.NS_OK:
                 raise RuntimeError(f"ns_vp_local failed: {_lib.status_string(rc)}")
-            gathered = gather_records(rec, self.group)
-            rc = self.lib.ns_vp_merge(
-                gathered.data_ptr(), self.world, B, cap, self.vocab_total,
-                st.p32, st.p32 + 4 * B, st.p32 + 8 * B, st.u_ptr, self.seed, offset,
-                out.data_ptr(), stream.cuda_stream)
+            if peer:
+                flags, _keep1 = _ptr_array([ex.flags(r) for r in range(self.world)])
+                rc = self.lib.ns_vp_signal(flags, self.world, self.rank, ex.counter(), stream.cuda_stream)
+                if rc != _lib.NS_OK:
+                    raise RuntimeError(f"ns_vp_signal failed: {_lib.status_string(rc)}")
+                recs, _keep2 = _ptr_array([ex.record(r, par) for r in range(self.world)])
+                rc = self.lib.ns_vp_merge_peers(
+                    recs, self.world, ex.flags(self.rank), ex.counter(), B, cap, self.vocab_total,
+                    st.p32, st.p32 + 4 * B, st.p32 + 8 * B, st.u_ptr, self.seed, offset,
+                    out.data_ptr(), stream.cuda_stream)
+            else:
+                gathered = gather_records(rec, self.group)
+                rc = self.lib.ns_vp_merge(
+                    gathered.data_ptr(), self.world, B, cap, self.vocab_total,
+                    st.p32, st.p32 + 4 * B, st.p32 + 8 * B, st.u_ptr, self.seed, offset,
+                    out.data_ptr(), stream.cuda_stream)
             st.keep_alive(stream)
             if rc != _lib.NS_OK:
                 raise RuntimeError(f"ns_vp_merge failed: {_lib.status_string(rc)}")

@@ -113,6 +113,29 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// System-scope flag protocol between GPUs (peer memory over NVLink): the
+// writer fences its prior writes and releases the flag; a reader acquires it.
+__device__ __forceinline__ int64_t ld_acquire_sys(const int64_t* p) {
+  int64_t v;
+  asm volatile("ld.acquire.sys.global.s64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(int64_t* p, int64_t v) {
+  asm volatile("st.release.sys.global.s64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Wait until *p >= target; false if that did not happen within kWaitTimeoutNs.
+__device__ __forceinline__ bool flag_wait_bounded(const int64_t* p, int64_t target) {
+  if (ld_acquire_sys(p) >= target) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire_sys(p) >= target) return true;
+    if (global_timer_ns() - t0 > kWaitTimeoutNs) return false;
+  }
+}
+
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -120,7 +143,7 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
 }
 
 // 1-D bulk copy global -> this CTA's shared memory, completing on `bar`.
-// dst and src 16-byte aligned, bytes a multiple of 16.  No multicast.
+// dst and src 16-byte aligned, bytes a multiple of 16; this CTA only.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
                                          uint64_t policy) {
   asm volatile(

@@ -3633,12 +3633,40 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
 // and the result equals the single-device call on the whole row.
 // ---------------------------------------------------------------------------
 
+constexpr int kMaxPeers = 8;  // ranks of a peer-memory exchange (one NVLink domain)
+
 struct VpMerge {
-  const int64_t* rec;
+  const int64_t* rec;                // n_ranks consecutive records, or null:
+  const int64_t* peer[kMaxPeers];    // ... rank r's record read in place (peer memory)
+  const int64_t* flags;              // null, or this rank's flags: wait for flags[r] >= *epoch
+  const int64_t* epoch;              // this rank's step counter (set by vp_signal_kernel)
   int n_ranks;
   int cap;
   int64_t batch;
 };
+
+struct VpSignal {
+  int64_t* flags[kMaxPeers];  // rank r's flag array (peer memory for r != me)
+  int64_t* epoch;             // this rank's step counter (device memory)
+  int n_ranks;
+  int me;
+};
+
+// After this rank's local step (the previous kernel on the stream): the step
+// counter advances and every rank's flags[me] = the new count, released at
+// system scope.  The count lives in device memory so that a captured CUDA
+// graph advances it on every replay.
+__global__ void vp_signal_kernel(const __grid_constant__ VpSignal s) {
+  const int r = threadIdx.x;
+  int64_t e = 0;
+  if (r == 0) {
+    e = *s.epoch + 1;
+    *s.epoch = e;
+  }
+  e = __shfl_sync(0xFFFFFFFFu, e, 0);
+  __threadfence_system();
+  if (r < s.n_ranks) st_release_sys(s.flags[r] + s.me, e);
+}
 
 __device__ __forceinline__ int status_rank(int64_t st) {  // single-device priority order
   switch (int(st)) {
@@ -3671,11 +3699,22 @@ __global__ void __launch_bounds__(kThreads) vp_merge_kernel(const __grid_constan
   c.u_pre = a.uniforms ? a.uniforms[row] : 0.0f;
   Misc* m = c.m;
   const int64_t rlen = v.batch * (1 + int64_t(v.cap));
+  auto record = [&](int r) { return v.rec ? v.rec + r * rlen : v.peer[r]; };
+  if (v.flags) {  // peer records: wait (bounded) until every rank has signalled this step
+    if (tid == 0) m->r_digit = 0;
+    __syncthreads();
+    if (tid < v.n_ranks && !flag_wait_bounded(v.flags + tid, *v.epoch)) atomicOr(&m->r_digit, 1);
+    __syncthreads();
+    if (m->r_digit) {
+      if (tid == 0) a.out_ids[row] = NS_ERR_DEVICE_TIMEOUT;
+      return;
+    }
+  }
   if (tid == 0) {
     int64_t err = 0;
     int tot = 0;
     for (int r = 0; r < v.n_ranks; ++r) {
-      const int64_t h = v.rec[r * rlen + row];
+      const int64_t h = record(r)[row];
       m->roff[r] = tot;
       if (h < 0) {
         if (err == 0 || status_rank(h) < status_rank(err)) err = h;
@@ -3695,7 +3734,7 @@ __global__ void __launch_bounds__(kThreads) vp_merge_kernel(const __grid_constan
     if (warp == 0) {
       uint64_t best = 0;
       for (int r = lane; r < v.n_ranks; r += 32) {
-        const int64_t* base = v.rec + r * rlen;
+        const int64_t* base = record(r);
         if (base[row] > 0) best = max(best, uint64_t(base[v.batch + row * v.cap]));
       }
 #pragma unroll
@@ -3722,7 +3761,7 @@ __global__ void __launch_bounds__(kThreads) vp_merge_kernel(const __grid_constan
   uint64_t* sorted = reinterpret_cast<uint64_t*>(c.stages + kRankKeysOff) + kRankMax;
   for (int r = warp; r < v.n_ranks; r += kWarps) {
     const int cnt = m->roff[r + 1] - m->roff[r];
-    const int64_t* src = v.rec + r * rlen + v.batch + row * v.cap;
+    const int64_t* src = record(r) + v.batch + row * v.cap;
     for (int i = lane; i < cnt; i += 32) lists[m->roff[r] + i] = uint64_t(src[i]);
   }
   __syncthreads();
@@ -4006,12 +4045,106 @@ int ns_vp_merge(const int64_t* gathered, int n_ranks, int64_t batch, int cap, in
   a.offset = philox_offset;
   a.out_ids = out_ids;
   a.merge_cap = ns::kMergeCap;
-  ns::VpMerge v;
+  ns::VpMerge v = {};
   v.rec = gathered;
   v.n_ranks = n_ranks;
   v.cap = cap;
   v.batch = batch;
   return ns::vp_merge_launch(a, v, stream);
+}
+
+int ns_vp_merge_peers(const int64_t* const* rank_records, int n_ranks, const int64_t* my_flags,
+                      const int64_t* epoch, int64_t batch, int cap, int64_t vocab_total, const float* temperature,
+                      const int32_t* top_k, const float* top_p, const float* uniforms, uint64_t philox_seed,
+                      uint64_t philox_offset, int64_t* out_ids, ns_stream_t stream) {
+  if (n_ranks < 1 || n_ranks > ns::kMaxPeers || batch < 0 || cap < 1 || cap > ns::kRankMax || !epoch)
+    return NS_ERR_INVALID_ARGUMENT;
+  if (vocab_total <= 0 || vocab_total > (int64_t(1) << 24) || batch > (int64_t(1) << 24)) return NS_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return NS_OK;
+  if (!rank_records || !my_flags || !temperature || !top_k || !top_p || !out_ids) return NS_ERR_INVALID_ARGUMENT;
+  ns::KArgs a = {};
+  a.vocab = vocab_total;
+  a.vocab_offset = 0;
+  a.vocab_total = vocab_total;
+  a.temperature = temperature;
+  a.top_k = top_k;
+  a.top_p = top_p;
+  a.uniforms = uniforms;
+  a.seed = philox_seed;
+  a.offset = philox_offset;
+  a.out_ids = out_ids;
+  a.merge_cap = ns::kMergeCap;
+  ns::VpMerge v = {};
+  v.rec = nullptr;
+  for (int r = 0; r < n_ranks; ++r) {
+    if (!rank_records[r]) return NS_ERR_INVALID_ARGUMENT;
+    v.peer[r] = rank_records[r];
+  }
+  v.flags = my_flags;
+  v.epoch = epoch;
+  v.n_ranks = n_ranks;
+  v.cap = cap;
+  v.batch = batch;
+  return ns::vp_merge_launch(a, v, stream);
+}
+
+int ns_vp_signal(int64_t* const* rank_flags, int n_ranks, int my_rank, int64_t* epoch, ns_stream_t stream) {
+  if (!rank_flags || n_ranks < 1 || n_ranks > ns::kMaxPeers || my_rank < 0 || my_rank >= n_ranks || !epoch)
+    return NS_ERR_INVALID_ARGUMENT;
+  ns::VpSignal sg = {};
+  for (int r = 0; r < n_ranks; ++r) {
+    if (!rank_flags[r]) return NS_ERR_INVALID_ARGUMENT;
+    sg.flags[r] = rank_flags[r];
+  }
+  sg.n_ranks = n_ranks;
+  sg.me = my_rank;
+  sg.epoch = epoch;
+  ns::vp_signal_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(sg);
+  return cudaGetLastError() == cudaSuccess ? NS_OK : NS_ERR_CUDA;
+}
+
+int ns_vp_peer_alloc(size_t bytes, void** out_ptr) {
+  if (!out_ptr || bytes == 0) return NS_ERR_INVALID_ARGUMENT;
+  *out_ptr = nullptr;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return NS_ERR_CUDA;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(p);
+    return NS_ERR_CUDA;
+  }
+  *out_ptr = p;
+  return NS_OK;
+}
+
+int ns_vp_peer_free(void* ptr) {
+  if (!ptr) return NS_OK;
+  return cudaFree(ptr) == cudaSuccess ? NS_OK : NS_ERR_CUDA;
+}
+
+static_assert(sizeof(cudaIpcMemHandle_t) == NS_IPC_HANDLE_BYTES, "IPC handle size");
+
+int ns_ipc_handle(const void* ptr, void* out_handle) {
+  if (!ptr || !out_handle) return NS_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)) != cudaSuccess) return NS_ERR_CUDA;
+  std::memcpy(out_handle, &h, sizeof(h));
+  return NS_OK;
+}
+
+int ns_ipc_open(const void* handle, void** out_ptr) {
+  if (!handle || !out_ptr) return NS_ERR_INVALID_ARGUMENT;
+  *out_ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return NS_ERR_CUDA;
+  *out_ptr = p;
+  return NS_OK;
+}
+
+int ns_ipc_close(void* ptr) {
+  if (!ptr) return NS_OK;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? NS_OK : NS_ERR_CUDA;
 }
 
 }  // extern "C"

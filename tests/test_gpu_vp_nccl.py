@@ -1,8 +1,11 @@
-"""Vocab-parallel sampling across real GPUs: one process per GPU over NCCL.
+"""Vocab-parallel sampling across real GPUs: one process per GPU.
 
 Each rank holds a column slice of every row; ``VocabParallelSampler`` must
-return, on every rank, the ids ``B200Sampler`` returns on the whole rows.
-Skipped when fewer than two GPUs are visible.
+return, on every rank, the ids ``B200Sampler`` returns on the whole rows, over
+several consecutive steps (the peer exchange alternates its two record
+buffers), with the records read in place over NVLink (``peer``) or
+all-gathered (``gather``).  A one-rank group runs the peer path (flags,
+epochs, record parity) on a single GPU.
 """
 import datetime
 import os
@@ -22,7 +25,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, errq):
+def _worker(rank, world, port, errq, transports=("peer", "gather"), steps=3):
     try:
         import torch.distributed as dist
         from b200_sampler import B200Sampler, VocabParallelSampler
@@ -48,14 +51,26 @@ def _worker(rank, world, port, errq):
                 params.append(SamplingParams(temperature=float(rng.choice([0.7, 1.2])),
                                              top_k=int(rng.choice([10, 50, 100])), top_p=0.9,
                                              repetition_penalty=1.1, presence_penalty=0.5))
-        u = make_uniforms(54, B)
         w = (V + world - 1) // world
         off = rank * w
         width = min(w, V - off)
-        vps = VocabParallelSampler(V, off, width, seed=9)
-        got = vps.select_batch(x[:, off:off + width].to(dev), hs, params, uniforms=u.to(dev))
-        ref = B200Sampler(seed=9).select_batch(x.to(dev), hs, params, uniforms=u.to(dev))
-        assert got == ref, (rank, [(b, g, r) for b, (g, r) in enumerate(zip(got, ref)) if g != r][:5])
+        xs = x[:, off:off + width].to(dev)
+        ref_sampler = B200Sampler(seed=9)
+        for transport in transports:
+            vps = VocabParallelSampler(V, off, width, seed=9, transport=transport)
+            assert vps.transport == transport
+            for step in range(steps):
+                u = make_uniforms(54 + step, B)
+                if step == 2:   # larger records: the peer buffers grow collectively
+                    ps = [SamplingParams(temperature=0.8, top_k=200, top_p=0.95, repetition_penalty=1.1)
+                          for _ in range(B)]
+                else:
+                    ps = params
+                got = vps.select_batch(xs, hs, ps, uniforms=u.to(dev))
+                ref = ref_sampler.select_batch(x.to(dev), hs, ps, uniforms=u.to(dev))
+                assert got == ref, (rank, transport, step,
+                                    [(b, g, r) for b, (g, r) in enumerate(zip(got, ref)) if g != r][:5])
+            vps.close()
         dist.barrier()
         dist.destroy_process_group()
     except BaseException as e:
@@ -63,15 +78,11 @@ def _worker(rank, world, port, errq):
         raise
 
 
-def test_vocab_parallel_nccl():
-    n = torch.cuda.device_count()
-    if n < 2:
-        pytest.skip("needs two or more GPUs")
-    world = min(n, 8)
+def _spawn(world, **kw):
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, errq)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, errq), kwargs=kw) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -85,3 +96,14 @@ def test_vocab_parallel_nccl():
     assert not alive, "a rank did not finish"
     assert not errs, errs
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+
+def test_vocab_parallel_one_rank_peer():
+    _spawn(1, transports=("peer",), steps=4)
+
+
+def test_vocab_parallel_nccl():
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs two or more GPUs")
+    _spawn(min(n, 8))
