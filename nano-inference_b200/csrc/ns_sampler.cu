@@ -156,6 +156,10 @@ struct Misc {
   int w_bin;                // wide NUCLEUS: last bin of the candidate set
   int w_n;                  // ... its count, and the keys collected
   int w_tot;                // ... values counted in the window
+  int w_binb;               // large nucleus: the bin where the exact mass crosses p Z
+  int w_cntb;               // ... and its count
+  unsigned long long w_keyL;  // large nucleus: the last kept key of the boundary bin
+  int w_L;                  // ... and how many of its keys are kept (-1: none / fall back)
   int roff[kMaxLists + 1];  // leader: union offsets over (rank, warp) lists
   int rc0[kMaxCluster];     // leader: first column of each rank
   uint32_t hist[kBins];
@@ -2629,22 +2633,22 @@ __device__ void cluster_digit(cg::cluster_group& cl, int CL, Misc* m, const unsi
 // values, and 16-byte groups holding only such values, are skipped) and
 // collects those of the first kb bins as keys (f2key(y) << 32 | ~id, y =
 // rn(x / |T|)).  M, Z: the row's largest scaled value and total mass from the
-// stream; D = dk + 4.5 and the keys' window dk + 3.5 nats, dk the kNucleusK-th
-// largest value's distance from M.  A value in bin b weighs at least
-// e^-(b+1) D / 255 (less a margin for the rounding), so the smallest bin
-// prefix whose guaranteed mass exceeds (p + 1e-6) Z holds the nucleus.  No
-// such prefix: the pass repeats with D doubled (at most 32 nats) and keys from
-// every bin (unless the window already counts more than kWideCap values).  A
-// prefix past the keys' bins, or more than kWideCap keys: one more pass
-// collects that prefix alone.
+// stream; D = dk + 4.5 and the keys' window dk + 3.5 nats, dk the
+// kNucleusK-th largest value's distance from M.  On the first pass a value in
+// bin b weighs at least e^-(b+1) D / 255 (less a margin for the rounding), so
+// the smallest bin prefix whose guaranteed mass exceeds (p + 1e-6) Z holds
+// the nucleus; later passes (a wider window, or the same one when the prefix
+// holds more values than the keys) sum exact 2^-40 fixed-point masses per bin
+// instead.  A prefix past the keys' bins, or more than kWideCap keys: one more
+// pass collects that prefix alone; a prefix past kWideCap values: the large
+// nucleus path (nucleus_big) with the bin where the exact mass crosses p Z.
 // The collected set is an upper set of x, so every value scaled above its
 // smallest y is in it; the keys are sorted (by bucket of y, then rank), and
 // when those values alone hold more than (p + 1e-6) Z (float64 sums) the
 // top-p cut lies before the smallest y: the cut and the draw run on the keys
 // with Z as the softmax normaliser (reference sampler.py:122-131, 86-89).
 // Returns false -- the same on every thread -- when the row continues on the
-// multi-pass path (prefix over kWideCap values, failed check); true when its
-// result is written.
+// multi-pass path; true when its result is written.
 // ---------------------------------------------------------------------------
 constexpr int kWideBins = kBins;  // 255 window bins + the deeper values
 constexpr float kWideMaxNats = 32.0f;
@@ -2668,6 +2672,258 @@ __device__ __forceinline__ float wide_floor(float M, float dd, float Tabs) {
   return b - (fabsf(M) + dd) * Tabs * 0x1p-18f - 1e-30f;
 }
 
+// NUCLEUS rows whose nucleus holds more values than the keys fit (one CTA):
+// the window's bin jb holds the cut.  One more pass sums the exact masses of
+// bins < jb per tile (2^-40 fixed point, as the multi-pass path) and collects
+// bin jb alone as keys; the sorted keys give the cut (keep position j while
+// the mass before it is at most p Z, reference sampler.py:122-131), the kept
+// keys are added to their tiles, and the draw locates its tile and scans it
+// again in id order (a value is kept iff its bin is below jb, or it is in bin
+// jb with a key at or above the last kept key).  Returns false (the same on
+// every thread) when the row continues on the multi-pass path: bin jb over
+// kWideCap values, the exact mass of bins < jb already past p Z, or a tie at
+// the cut that may reach into a neighbouring bin.
+template <int DT>
+__device__ bool nucleus_big(const Ctx<DT>& c, const KArgs& a, int& seq, uint64_t policy, float topp, float M,
+                            double Z, float r, float S, int jb) {
+  constexpr int VE = Ctx<DT>::VE, TE = Ctx<DT>::TE;
+  Misc* m = c.m;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint64_t* keys = reinterpret_cast<uint64_t*>(c.cx);
+  unsigned long long* tmass = reinterpret_cast<unsigned long long*>(c.tacc);
+  auto yof = [&](float x) { return __fdiv_rn(x, c.Tabs) + 0.0f; };  // -0 and +0 tie
+  auto wfx = [&](float y) { return to_fx(expf(__fsub_rn(y, M))); };
+  auto key_of = [&](float x, int col) {
+    return (uint64_t(f2key(yof(x))) << 32) | uint64_t(~uint32_t(c.c0 + col));
+  };
+  if (tid == 0) m->w_n = 0;
+  __syncthreads();
+  {
+    unsigned long long acc = 0;
+    warp_pass(
+        c, seq, 0, policy, c.rep, c.pres, c.freq,
+        [&](float x, int col) {
+          if (!(x > -INFINITY)) return;
+          const int b = wide_bin(x, M, r, S);
+          if (b < jb) {
+            acc += wfx(yof(x));
+          } else if (b == jb) {
+            const int i = atomicAdd(&m->w_n, 1);
+            if (i < kWideCap) keys[i] = key_of(x, col);
+          }
+        },
+        [&](int t) {
+          const unsigned long long sum = warp_sum_u64(acc);
+          acc = 0;
+          if (lane == 0) tmass[warp * c.tpw + t] = sum;
+        },
+        wide_floor(M, float(jb + 1) / S, c.Tabs));
+  }
+  __syncthreads();
+  if (m->flags & F_TIMEOUT) {
+    if (tid == 0) a.out_ids[c.row] = NS_ERR_DEVICE_TIMEOUT;
+    return true;
+  }
+  const int n = m->w_n;
+  if (n > kWideCap || n == 0) return false;
+  // the exact mass of bins < jb
+  auto block_sum_u64 = [&](unsigned long long v) {
+    v = warp_sum_u64(v);
+    if (lane == 0) m->g_sum[warp] = v;
+    __syncthreads();
+    unsigned long long t = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) t += m->g_sum[w];
+    __syncthreads();
+    return t;
+  };
+  auto tile_sum = [&]() {
+    unsigned long long v = 0;
+    for (int w = 0; w < kWarps; ++w)
+      for (int t = tid; t < c.wtiles(w); t += kThreads) v += tmass[w * c.tpw + t];
+    return block_sum_u64(v);
+  };
+  const unsigned long long A = tile_sum();
+  // bin jb's keys in descending order (sub-buckets of the bin by scaled value)
+  uint64_t* tmp = reinterpret_cast<uint64_t*>(c.stages + size_t(kMergeCap) * 8);
+  uint64_t* sorted = reinterpret_cast<uint64_t*>(c.stages + kRankKeysOff) + kRankMax;
+  bucket_sort(
+      m, keys, n, tmp, sorted,
+      [&](uint64_t k) {
+        const float d = ((M - key2f(uint32_t(k >> 32))) * S - float(jb)) * float(kBins - 1);
+        return d < float(kBins - 1) ? int(fmaxf(d, 0.0f)) : kBins - 1;
+      },
+      [](uint64_t x, uint64_t y) { return x > y; });
+  // the cut: L = the first position whose preceding mass exceeds p Z
+  const unsigned long long target = (unsigned long long)(double(topp) * (Z * kFx));
+  if (warp == 0) {
+    const int per = (n + 31) / 32;
+    const int i0 = min(lane * per, n), i1 = min(i0 + per, n);
+    unsigned long long loc = 0;
+    for (int i = i0; i < i1; ++i) loc += wfx(key2f(uint32_t(sorted[i] >> 32)));
+    unsigned long long ex = loc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned long long v = __shfl_up_sync(kFull, ex, o);
+      if (lane >= o) ex += v;
+    }
+    ex -= loc;
+    unsigned long long cum = A + ex;
+    int first = INT_MAX;
+    for (int i = i0; i < i1 && first == INT_MAX; ++i) {
+      if (cum > target) first = i;
+      cum += wfx(key2f(uint32_t(sorted[i] >> 32)));
+    }
+    first = int(__reduce_min_sync(kFull, unsigned(first)));
+    if (lane == 0) {
+      const int L = first;  // kept: sorted[0, L)
+      const uint32_t yL = (L >= 1 && L < n) ? uint32_t(sorted[L - 1] >> 32) : 0u;
+      // a tie at the cut must not reach into the bins around jb
+      const bool ok = L >= 1 && L < n && !(jb > 0 && yL == uint32_t(sorted[0] >> 32)) &&
+                      yL != uint32_t(sorted[n - 1] >> 32);
+      m->w_L = ok ? L : -1;
+      m->w_keyL = ok ? sorted[L - 1] : 0ull;
+    }
+  }
+  __syncthreads();
+  const int L = m->w_L;
+  const uint64_t keyL = m->w_keyL;
+  if (L < 0) return false;
+  // kept keys by ascending id, their masses added to their tiles
+  {
+    uint64_t* byid = reinterpret_cast<uint64_t*>(c.stages);
+    for (int i = tid; i < L; i += kThreads) {
+      const uint64_t k = sorted[i];
+      tmp[i] = (uint64_t(~uint32_t(k)) << 32) | (k >> 32);  // (id, y key)
+    }
+    __syncthreads();
+    int sh = 0;
+    while ((int64_t(c.c1) - 1) >> (8 + sh)) ++sh;  // call-local ids < c1
+    bucket_sort(
+        m, tmp, L, sorted, byid, [&](uint64_t k) { return int(uint32_t(k >> 32) >> sh); },
+        [](uint64_t x, uint64_t y) { return x < y; });
+    auto lower = [&](uint32_t id) {  // first kept key with id >= id
+      int lo = 0, hi = L;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (uint32_t(byid[mid] >> 32) < id)
+          lo = mid + 1;
+        else
+          hi = mid;
+      }
+      return lo;
+    };
+    for (int w = 0; w < kWarps; ++w)
+      for (int t = tid; t < c.wtiles(w); t += kThreads) {
+        const uint32_t col0 = uint32_t(c.c0 + w * c.pw + t * TE);
+        const int i0 = lower(col0), i1 = lower(col0 + uint32_t(c.tile_len(w, t)));
+        unsigned long long add = 0;
+        for (int i = i0; i < i1; ++i) add += wfx(key2f(uint32_t(byid[i])));
+        tmass[w * c.tpw + t] += add;
+      }
+  }
+  __syncthreads();
+  const unsigned long long W = tile_sum();
+  // the tile holding u * W (the last kept tile if rounding leaves it past the end)
+  const float u = a.uniforms ? c.u_pre : philox_uniform(a.seed, a.offset, uint64_t(c.row));
+  const unsigned long long tgt = (unsigned long long)(double(u) * double(W));
+  if (tid == 0) {
+    int tsel = -1, tlast = -1;
+    unsigned long long before = 0, run = 0;
+    for (int w = 0; w < kWarps; ++w)
+      for (int t = 0; t < c.wtiles(w); ++t) {
+        const int gt = w * c.tpw + t;
+        if (tmass[gt] > 0) tlast = gt;
+        if (tsel < 0 && run + tmass[gt] > tgt) {
+          tsel = gt;
+          before = run;
+        }
+        run += tmass[gt];
+      }
+    m->g_bin = 0;
+    if (tsel < 0) {
+      tsel = tlast;
+      m->g_bin = 1;
+    }
+    m->g_tile = tsel;
+    m->g_tbefore = before;
+  }
+  __syncthreads();
+  const int gsel = m->g_tile;
+  if (gsel < 0) {
+    if (tid == 0) a.out_ids[c.row] = NS_ERR_INVALID_DISTRIBUTION;
+    return true;
+  }
+  if (warp != gsel / c.tpw) return true;
+  // this warp copies its tile again and scans it in id order
+  const int t = gsel % c.tpw;
+  const bool pe = m->g_bin != 0;
+  const unsigned long long tbefore = m->g_tbefore;
+  const int sidx = seq % kWStages;
+  if (lane == 0) issue_tile(c, warp, t, sidx, policy);
+  if (!__all_sync(kFull, mbar_wait_bounded(c.sbar(warp, sidx), uint32_t(seq / kWStages) & 1u))) {
+    if (lane == 0) a.out_ids[c.row] = NS_ERR_DEVICE_TIMEOUT;
+    return true;
+  }
+  uint8_t* st = c.stage(warp, sidx);
+  float* F = reinterpret_cast<float*>(c.cx);  // the tile's values in column order (keys are dead)
+  const int len = c.tile_len(warp, t), lead = c.tile_lead(warp, t);
+  const int n_groups = (lead + len + VE - 1) / VE;
+  const int base = warp * c.pw + t * TE;
+  for (int q = lane; q < n_groups; q += 32) {
+    float x[VE];
+    unpack16<DT>(*reinterpret_cast<const uint4*>(st + q * 16), x);
+#pragma unroll
+    for (int i = 0; i < VE; ++i) {
+      const int e = q * VE + i;
+      if (e >= lead && e < lead + len) F[e - lead] = c.neg ? -x[i] : x[i];
+    }
+  }
+  __syncwarp();
+  patch_tile(c, warp, t, st, [&](bool has, float xp, int col) {  // history columns: penalised values
+    if (has) F[col - base] = xp;
+  });
+  __syncwarp();
+  auto mass_of = [&](int i) -> unsigned long long {
+    const float x = F[i];
+    if (!(x > -INFINITY)) return 0ull;
+    const int b = wide_bin(x, M, r, S);
+    if (b > jb || (b == jb && key_of(x, base + i) < keyL)) return 0ull;
+    return wfx(yof(x));
+  };
+  const int per = (len + 31) / 32;
+  const int i0 = min(lane * per, len), i1 = min(i0 + per, len);
+  unsigned long long lm = 0;
+  for (int i = i0; i < i1; ++i) lm += mass_of(i);
+  unsigned long long ex = lm;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned long long v = __shfl_up_sync(kFull, ex, o);
+    if (lane >= o) ex += v;
+  }
+  ex -= lm;
+  unsigned long long cum = tbefore + ex;
+  int pick = -1, last = -1;
+  for (int i = i0; i < i1; ++i) {
+    const unsigned long long e = mass_of(i);
+    if (e == 0) continue;
+    last = i;
+    if (pick < 0 && !pe && cum + e > tgt) pick = i;
+    cum += e;
+  }
+  const unsigned pm = __ballot_sync(kFull, pick >= 0);
+  int col = -1;
+  if (pm) {
+    col = __shfl_sync(kFull, pick, __ffs(pm) - 1);
+  } else {
+    const unsigned lmk = __ballot_sync(kFull, last >= 0);
+    if (lmk) col = __shfl_sync(kFull, last, 31 - __clz(lmk));
+  }
+  if (lane == 0)
+    a.out_ids[c.row] = (col >= 0) ? int64_t(c.c0 + base + col) + a.vocab_offset : int64_t(NS_ERR_INVALID_DISTRIBUTION);
+  return true;
+}
+
 template <int DT>
 __device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t policy, float topp) {
   Misc* m = c.m;
@@ -2676,6 +2932,7 @@ __device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t poli
   const double Z = m->nuc_Z;
   const float r = __frcp_rn(c.Tabs);
   uint32_t* h = m->hist;
+  unsigned long long* hm = reinterpret_cast<unsigned long long*>(c.tacc);  // exact masses per bin
   uint64_t* keys = reinterpret_cast<uint64_t*>(c.cx);
   auto key_of = [&](float x, int col) {
     const float y = __fdiv_rn(x, c.Tabs) + 0.0f;  // -0 and +0 tie
@@ -2684,13 +2941,18 @@ __device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t poli
   const float dk = __fsub_rn(M, m->nuc_yk);  // +inf when unknown
   float D = fminf(dk + 4.5f, kWideMaxNats);
   float S = 0.0f;
-  int jb = INT_MAX, nb = 0, n = 0, kb = 0;
-  for (int att = 0;; ++att) {
+  int jb = INT_MAX, nb = 0, n = 0, kb = 0, jg = INT_MAX, ng = 0;
+  bool keyless = false;  // the window already counts more values than the keys hold
+  bool exact = false;    // this attempt sums exact masses per bin (else guaranteed lower bounds)
+  for (int att = 0; att < 6; ++att) {
     S = float(kWideBins - 1) / D;
     kb = (att == 0) ? int(fminf((dk + 3.5f) * S, float(kWideBins - 1))) : kWideBins - 1;  // NaN: all
+    if (keyless) kb = 0;
     h[tid] = 0u;
+    hm[tid] = 0ull;
     if (tid == 0) {
       m->w_bin = INT_MAX;
+      m->w_binb = INT_MAX;
       m->w_n = 0;
     }
     __syncthreads();
@@ -2701,6 +2963,7 @@ __device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t poli
             const int b = wide_bin(x, M, r, S);
             if (b < kWideBins - 1) {
               atomicAdd(&h[b], 1u);
+              if (exact) atomicAdd(&hm[b], to_fx(expf(__fsub_rn(__fdiv_rn(x, c.Tabs) + 0.0f, M))));
               if (b < kb) {
                 const int i = atomicAdd(&m->w_n, 1);
                 if (i < kWideCap) keys[i] = key_of(x, col);
@@ -2715,45 +2978,74 @@ __device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t poli
       return true;
     }
     n = m->w_n;
-    // the smallest prefix of bins whose guaranteed mass exceeds the target
+    // The bin where the cumulative mass first exceeds (p + 1e-6) Z by the
+    // guaranteed lower bounds, or, with exact masses (2^-40 fixed point),
+    // (p + 2e-6) Z -- the keys' prefix, which then passes the float64 check --
+    // and p Z, the large-nucleus cut.
     const int cnt = (tid < kWideBins - 1) ? int(h[tid]) : 0;
+    const unsigned long long ms = (tid < kWideBins - 1 && exact) ? hm[tid] : 0ull;
     const double lm = double(cnt) * double(expf(-(float(tid) + 1.0f) * (D / float(kWideBins - 1)) - 1e-4f));
-    double im = lm;
+    unsigned long long im = ms;
+    double il = lm;
     int ic = cnt;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const double vm = __shfl_up_sync(kFull, im, o);
+      const unsigned long long vm = __shfl_up_sync(kFull, im, o);
+      const double vl = __shfl_up_sync(kFull, il, o);
       const int vc = __shfl_up_sync(kFull, ic, o);
       if (lane >= o) {
         im += vm;
+        il += vl;
         ic += vc;
       }
     }
     if (lane == 31) {
-      m->d_red[warp] = im;
+      m->g_sum[warp] = im;
+      m->d_red[warp] = il;
       m->i_red[warp] = ic;
     }
     __syncthreads();
     for (int w = 0; w < warp; ++w) {  // never reads the last warp's entries
-      im += m->d_red[w];
+      im += m->g_sum[w];
+      il += m->d_red[w];
       ic += m->i_red[w];
     }
-    const double target = (double(topp) + 1e-6) * Z;
-    if (im > target && im - lm <= target) {  // one thread at most
-      m->w_bin = tid;
-      m->i_red[kWarps - 1] = ic;
+    if (exact) {
+      const unsigned long long tk = (unsigned long long)((double(topp) + 2e-6) * (Z * kFx));
+      const unsigned long long tg = (unsigned long long)(double(topp) * (Z * kFx));
+      if (im > tk && im - ms <= tk) {  // one thread at most
+        m->w_bin = tid;
+        m->i_red[kWarps - 1] = ic;
+      }
+      if (im > tg && im - ms <= tg) {
+        m->w_binb = tid;
+        m->w_cntb = cnt;
+      }
+    } else {
+      const double target = (double(topp) + 1e-6) * Z;
+      if (il > target && il - lm <= target) {
+        m->w_bin = tid;
+        m->i_red[kWarps - 1] = ic;
+      }
     }
     if (tid == kThreads - 1) m->w_tot = ic;  // values counted in the window
     __syncthreads();
     jb = m->w_bin;
     nb = (jb != INT_MAX) ? m->i_red[kWarps - 1] : 0;
+    jg = m->w_binb;
+    ng = (jg != INT_MAX) ? m->w_cntb : 0;
     const int tot = m->w_tot;
     __syncthreads();
-    if (jb != INT_MAX || D >= kWideMaxNats) break;
-    if (tot > kWideCap) return false;  // any prefix that reaches the target is larger still
-    D = fminf(2.0f * D, kWideMaxNats);  // the window held too little mass: wider
+    if (jb != INT_MAX && nb <= kWideCap) break;  // the keys' prefix
+    if (exact && (jg != INT_MAX || D >= kWideMaxNats)) break;
+    keyless = keyless || tot > kWideCap;         // any prefix reaching the target is larger still
+    if (jb == INT_MAX && D < kWideMaxNats) D = fminf(2.0f * D, kWideMaxNats);  // too little mass: wider
+    exact = true;                                // later attempts sum exact masses
   }
-  if (jb == INT_MAX || nb > kWideCap || nb == 0) return false;
+  if (jb == INT_MAX || nb == 0 || nb > kWideCap) {  // no keys' prefix: the large-nucleus path
+    if (!exact || jg == INT_MAX || ng == 0 || ng > kWideCap) return false;
+    return nucleus_big(c, a, seq, policy, topp, M, Z, r, S, jg);
+  }
   if (jb >= kb || n > kWideCap) {  // the prefix lies past the keys' bins, or they overflowed
     if (tid == 0) m->w_n = 0;
     __syncthreads();
@@ -3801,8 +4093,8 @@ static Layout make_layout(int nwords, int cnt_cap, int n_tiles_all) {
   L.off_pval = o;
   o += uint32_t(cnt_cap) * 4;
   o = align_up(o, 16);
-  L.off_tacc = o;  // GENERAL: per-(warp, tile) mass (fixed point) and tie count
-  o += n_tiles_all * 12;
+  L.off_tacc = o;  // GENERAL: per-(warp, tile) mass (fixed point) and tie count; wide NUCLEUS: bin masses
+  o += std::max<uint32_t>(uint32_t(n_tiles_all) * 12, uint32_t(kWideBins) * 8);
   o = align_up(o, 16);
   L.off_misc = o;
   o += sizeof(Misc);
