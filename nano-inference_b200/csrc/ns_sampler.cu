@@ -153,6 +153,7 @@ struct Misc {
   float nuc_M;              // NUCLEUS: the row's largest scaled value
   double nuc_Z;             // ... and its total mass sum exp(y - nuc_M)
   float nuc_yk;             // ... and its kNucleusK-th largest scaled value (-inf: unknown)
+  float nuc_cov;            // ... and the share of the mass those hold (-1: unknown)
   int w_bin;                // wide NUCLEUS: last bin of the candidate set
   int w_n;                  // ... its count, and the keys collected
   int w_tot;                // ... values counted in the window
@@ -1995,6 +1996,7 @@ __device__ bool row_tail(const Ctx<DT>& c, const KArgs& a, cg::cluster_group& cl
         m->nuc_M = M;
         m->nuc_Z = Z;
         m->nuc_yk = -INFINITY;
+        m->nuc_cov = -1.0f;
       }
     }
     if ((fl1 & (F_OVF | F_BIG)) && !(fl1 & (F_NAN | F_TIMEOUT | F_BADID | F_HIST))) return false;
@@ -2016,6 +2018,7 @@ __device__ bool row_tail(const Ctx<DT>& c, const KArgs& a, cg::cluster_group& cl
         if (lane == 0 && !covered) {
           atomicOr(&m->flags, F_OVF);
           if (n > 0) m->nuc_yk = key2f(uint32_t(sorted[min(c.K, n) - 1] >> 32));
+          if (Z > 0.0) m->nuc_cov = float(cm / Z);
         }
       }
       __syncthreads();
@@ -2637,9 +2640,8 @@ __device__ void cluster_digit(cg::cluster_group& cl, int CL, Misc* m, const unsi
 // kNucleusK-th largest value's distance from M.  On the first pass a value in
 // bin b weighs at least e^-(b+1) D / 255 (less a margin for the rounding), so
 // the smallest bin prefix whose guaranteed mass exceeds (p + 1e-6) Z holds
-// the nucleus; later passes (a wider window, or the same one when the prefix
-// holds more values than the keys) sum exact 2^-40 fixed-point masses per bin
-// instead.  A prefix past the keys' bins, or more than kWideCap keys: one more
+// the nucleus; later passes (a window twice as wide, or the same one when the prefix
+// holds more values than the keys) sum each bin's masses (float) instead.  A prefix past the keys' bins, or more than kWideCap keys: one more
 // pass collects that prefix alone; a prefix past kWideCap values: the large
 // nucleus path (nucleus_big) with the bin where the exact mass crosses p Z.
 // The collected set is an upper set of x, so every value scaled above its
@@ -2672,6 +2674,32 @@ __device__ __forceinline__ float wide_floor(float M, float dd, float Tabs) {
   return b - (fabsf(M) + dd) * Tabs * 0x1p-18f - 1e-30f;
 }
 
+// Whether every x (the pass's domain) with rn(x / Tabs) == y falls in bin jb:
+// walks the float grid from y * Tabs to the ends of y's class; false (unsure)
+// when a walk takes more than 64 steps or y has no such x.
+__device__ bool y_class_in_bin(float y, float Tabs, float M, float r, float S, int jb) {
+  auto yq = [&](float x) { return __fdiv_rn(x, Tabs) + 0.0f; };
+  float x = y * Tabs;
+  for (int i = 0; i < 64 && yq(x) < y; ++i) x = nextafterf(x, INFINITY);
+  for (int i = 0; i < 64 && yq(x) > y; ++i) x = nextafterf(x, -INFINITY);
+  if (yq(x) != y) return false;
+  float lo = x, hi = x;
+  int i = 0;
+  for (; i < 64; ++i) {
+    const float nx = nextafterf(lo, -INFINITY);
+    if (yq(nx) != y) break;
+    lo = nx;
+  }
+  if (i == 64) return false;
+  for (i = 0; i < 64; ++i) {
+    const float nx = nextafterf(hi, INFINITY);
+    if (yq(nx) != y) break;
+    hi = nx;
+  }
+  if (i == 64) return false;
+  return wide_bin(lo, M, r, S) == jb && wide_bin(hi, M, r, S) == jb;
+}
+
 // NUCLEUS rows whose nucleus holds more values than the keys fit (one CTA):
 // the window's bin jb holds the cut.  One more pass sums the exact masses of
 // bins < jb per tile (2^-40 fixed point, as the multi-pass path) and collects
@@ -2681,8 +2709,8 @@ __device__ __forceinline__ float wide_floor(float M, float dd, float Tabs) {
 // again in id order (a value is kept iff its bin is below jb, or it is in bin
 // jb with a key at or above the last kept key).  Returns false (the same on
 // every thread) when the row continues on the multi-pass path: bin jb over
-// kWideCap values, the exact mass of bins < jb already past p Z, or a tie at
-// the cut that may reach into a neighbouring bin.
+// kWideCap values, the exact mass of bins < jb already past p Z, or values
+// tied with the cut that may lie in a neighbouring bin.
 template <int DT>
 __device__ bool nucleus_big(const Ctx<DT>& c, const KArgs& a, int& seq, uint64_t policy, float topp, float M,
                             double Z, float r, float S, int jb) {
@@ -2777,10 +2805,8 @@ __device__ bool nucleus_big(const Ctx<DT>& c, const KArgs& a, int& seq, uint64_t
     first = int(__reduce_min_sync(kFull, unsigned(first)));
     if (lane == 0) {
       const int L = first;  // kept: sorted[0, L)
-      const uint32_t yL = (L >= 1 && L < n) ? uint32_t(sorted[L - 1] >> 32) : 0u;
-      // a tie at the cut must not reach into the bins around jb
-      const bool ok = L >= 1 && L < n && !(jb > 0 && yL == uint32_t(sorted[0] >> 32)) &&
-                      yL != uint32_t(sorted[n - 1] >> 32);
+      // the values tied with the last kept one must all lie in bin jb
+      const bool ok = L >= 1 && L < n && y_class_in_bin(key2f(uint32_t(sorted[L - 1] >> 32)), c.Tabs, M, r, S, jb);
       m->w_L = ok ? L : -1;
       m->w_keyL = ok ? sorted[L - 1] : 0ull;
     }
@@ -2932,7 +2958,7 @@ __device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t poli
   const double Z = m->nuc_Z;
   const float r = __frcp_rn(c.Tabs);
   uint32_t* h = m->hist;
-  unsigned long long* hm = reinterpret_cast<unsigned long long*>(c.tacc);  // exact masses per bin
+  float* hm = reinterpret_cast<float*>(c.tacc);  // masses per bin (float: they only choose the bin)
   uint64_t* keys = reinterpret_cast<uint64_t*>(c.cx);
   auto key_of = [&](float x, int col) {
     const float y = __fdiv_rn(x, c.Tabs) + 0.0f;  // -0 and +0 tie
@@ -2943,13 +2969,18 @@ __device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t poli
   float S = 0.0f;
   int jb = INT_MAX, nb = 0, n = 0, kb = 0, jg = INT_MAX, ng = 0;
   bool keyless = false;  // the window already counts more values than the keys hold
-  bool exact = false;    // this attempt sums exact masses per bin (else guaranteed lower bounds)
+  bool exact = false;    // this attempt sums masses per bin (else guaranteed lower bounds)
+  const float cov = m->nuc_cov;
+  if (cov >= 0.0f && cov < 0.5f * topp) {  // the candidates hold little of the nucleus: it is far wider
+    D = fminf(2.0f * D, kWideMaxNats);
+    exact = true;
+  }
   for (int att = 0; att < 6; ++att) {
     S = float(kWideBins - 1) / D;
     kb = (att == 0) ? int(fminf((dk + 3.5f) * S, float(kWideBins - 1))) : kWideBins - 1;  // NaN: all
     if (keyless) kb = 0;
     h[tid] = 0u;
-    hm[tid] = 0ull;
+    hm[tid] = 0.0f;
     if (tid == 0) {
       m->w_bin = INT_MAX;
       m->w_binb = INT_MAX;
@@ -2963,7 +2994,7 @@ __device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t poli
             const int b = wide_bin(x, M, r, S);
             if (b < kWideBins - 1) {
               atomicAdd(&h[b], 1u);
-              if (exact) atomicAdd(&hm[b], to_fx(expf(__fsub_rn(__fdiv_rn(x, c.Tabs) + 0.0f, M))));
+              if (exact) atomicAdd(&hm[b], __expf(__fmul_rn(x, r) - M));
               if (b < kb) {
                 const int i = atomicAdd(&m->w_n, 1);
                 if (i < kWideCap) keys[i] = key_of(x, col);
@@ -2979,53 +3010,43 @@ __device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t poli
     }
     n = m->w_n;
     // The bin where the cumulative mass first exceeds (p + 1e-6) Z by the
-    // guaranteed lower bounds, or, with exact masses (2^-40 fixed point),
-    // (p + 2e-6) Z -- the keys' prefix, which then passes the float64 check --
-    // and p Z, the large-nucleus cut.
+    // guaranteed lower bounds, or, with summed masses, (p + 2e-6) Z -- the
+    // keys' prefix, which the float64 check then confirms -- and p Z, the
+    // large-nucleus cut (whose pass recomputes the masses exactly and falls
+    // back when the bin was not the right one).
     const int cnt = (tid < kWideBins - 1) ? int(h[tid]) : 0;
-    const unsigned long long ms = (tid < kWideBins - 1 && exact) ? hm[tid] : 0ull;
-    const double lm = double(cnt) * double(expf(-(float(tid) + 1.0f) * (D / float(kWideBins - 1)) - 1e-4f));
-    unsigned long long im = ms;
+    const double lm = exact ? double(hm[tid < kWideBins - 1 ? tid : 0]) * (tid < kWideBins - 1 ? 1.0 : 0.0)
+                            : double(cnt) * double(expf(-(float(tid) + 1.0f) * (D / float(kWideBins - 1)) - 1e-4f));
     double il = lm;
     int ic = cnt;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const unsigned long long vm = __shfl_up_sync(kFull, im, o);
       const double vl = __shfl_up_sync(kFull, il, o);
       const int vc = __shfl_up_sync(kFull, ic, o);
       if (lane >= o) {
-        im += vm;
         il += vl;
         ic += vc;
       }
     }
     if (lane == 31) {
-      m->g_sum[warp] = im;
       m->d_red[warp] = il;
       m->i_red[warp] = ic;
     }
     __syncthreads();
     for (int w = 0; w < warp; ++w) {  // never reads the last warp's entries
-      im += m->g_sum[w];
       il += m->d_red[w];
       ic += m->i_red[w];
     }
+    const double tk = (double(topp) + (exact ? 2e-6 : 1e-6)) * Z;
+    if (il > tk && il - lm <= tk) {  // one thread at most
+      m->w_bin = tid;
+      m->i_red[kWarps - 1] = ic;
+    }
     if (exact) {
-      const unsigned long long tk = (unsigned long long)((double(topp) + 2e-6) * (Z * kFx));
-      const unsigned long long tg = (unsigned long long)(double(topp) * (Z * kFx));
-      if (im > tk && im - ms <= tk) {  // one thread at most
-        m->w_bin = tid;
-        m->i_red[kWarps - 1] = ic;
-      }
-      if (im > tg && im - ms <= tg) {
+      const double tg = double(topp) * Z;
+      if (il > tg && il - lm <= tg) {
         m->w_binb = tid;
         m->w_cntb = cnt;
-      }
-    } else {
-      const double target = (double(topp) + 1e-6) * Z;
-      if (il > target && il - lm <= target) {
-        m->w_bin = tid;
-        m->i_red[kWarps - 1] = ic;
       }
     }
     if (tid == kThreads - 1) m->w_tot = ic;  // values counted in the window
@@ -3040,7 +3061,7 @@ __device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t poli
     if (exact && (jg != INT_MAX || D >= kWideMaxNats)) break;
     keyless = keyless || tot > kWideCap;         // any prefix reaching the target is larger still
     if (jb == INT_MAX && D < kWideMaxNats) D = fminf(2.0f * D, kWideMaxNats);  // too little mass: wider
-    exact = true;                                // later attempts sum exact masses
+    exact = true;                                // later attempts sum masses per bin
   }
   if (jb == INT_MAX || nb == 0 || nb > kWideCap) {  // no keys' prefix: the large-nucleus path
     if (!exact || jg == INT_MAX || ng == 0 || ng > kWideCap) return false;
