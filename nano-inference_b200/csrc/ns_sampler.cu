@@ -29,7 +29,11 @@
 //       and the draw run on them; otherwise (one CTA per row) one more pass
 //       collects a window of values below the row's maximum (nucleus_wide),
 //       else GENERAL.
-//   GENERAL (top-k > kFastK, ties overflowing a buffer, NUCLEUS rows whose
+//   WIDEK  (kFastK < top_k <= kWideCap, one CTA per row)
+//       FAST with kNucleusK candidates, then one more pass counting and
+//       collecting the values in a window below the row's maximum
+//       (wide_topk), else GENERAL.
+//   GENERAL (top-k beyond those, ties overflowing a buffer, NUCLEUS rows whose
 //       nucleus is larger)
 //       a cluster-cooperative multi-pass radix search over counts and
 //       fixed-point masses; the last pass rescans one tile in id order.
@@ -88,7 +92,7 @@ static_assert(kMergeCap * 16 <= kStageBytes, "merge lists and their sort keys fi
 constexpr int kMaxLists = kMaxCluster * kWarps;
 constexpr unsigned kFull = 0xFFFFFFFFu;
 
-enum : int { MODE_GREEDY = 0, MODE_FAST = 1, MODE_GENERAL = 2, MODE_SOFTMAX = 3, MODE_NUCLEUS = 4 };
+enum : int { MODE_GREEDY = 0, MODE_FAST = 1, MODE_GENERAL = 2, MODE_SOFTMAX = 3, MODE_NUCLEUS = 4, MODE_WIDEK = 5 };
 enum : int { F_NAN = 1, F_BADID = 2, F_HIST = 4, F_OVF = 8, F_TIMEOUT = 16, F_UNSUP = 32, F_BIG = 64 };
 
 // ---------------------------------------------------------------------------
@@ -1959,6 +1963,13 @@ __device__ bool row_tail(const Ctx<DT>& c, const KArgs& a, cg::cluster_group& cl
     if (nw & 1) keys[nw] = 0ull;  // pad to whole pairs
     m->wn[warp] = nw;
   }
+  if (mode == MODE_WIDEK) {  // this warp's largest scaled value (the sort below may not run)
+    uint64_t mk = 0;
+    for (int i = lane; i < nw; i += 32) mk = max(mk, keys[i]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mk = max(mk, __shfl_xor_sync(kFull, mk, o));
+    if (lane == 0) m->wbest[warp] = nw ? key2f(uint32_t(mk >> 32)) : -INFINITY;
+  }
   __syncthreads();
   int n = 0;
 #pragma unroll
@@ -1998,6 +2009,22 @@ __device__ bool row_tail(const Ctx<DT>& c, const KArgs& a, cg::cluster_group& cl
         m->nuc_yk = -INFINITY;
         m->nuc_cov = -1.0f;
       }
+    }
+    if (mode == MODE_WIDEK && !(fl1 & (F_NAN | F_TIMEOUT | F_BADID | F_HIST))) {
+      // the kNucleusK largest give the row's largest value and the window scale
+      if (tid == 0) {
+        float Mw = -INFINITY;
+        for (int w = 0; w < kWarps; ++w) Mw = fmaxf(Mw, m->wbest[w]);
+        const bool have = !(fl1 & F_OVF) && n > 0;  // no candidate buffer overflowed
+        m->nuc_M = have ? Mw : __int_as_float(0x7fc00000);  // NaN: unknown
+        // the kNucleusK-th largest: from the sorted union, else the tightest bound (below it)
+        m->nuc_yk = !have ? -INFINITY
+                          : (n <= kRankMax && n >= c.K) ? key2f(uint32_t(sorted[c.K - 1] >> 32))
+                                                        : __fdiv_rn(f.tau, c.Tabs);
+        atomicOr(&m->flags, F_OVF);
+      }
+      __syncthreads();
+      return false;
     }
     if ((fl1 & (F_OVF | F_BIG)) && !(fl1 & (F_NAN | F_TIMEOUT | F_BADID | F_HIST))) return false;
     const int st = status_from_flags(fl1, false);
@@ -3120,6 +3147,131 @@ __device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t poli
   return true;
 }
 
+// ---------------------------------------------------------------------------
+// Rows with kFastK < top_k <= kWideCap (one CTA per row).  The stream kept
+// the kNucleusK largest values (with ties): the first is the row's largest
+// scaled value M, the last sets the window scale dk.  One more pass counts the
+// values within D = dk + 4 nats of M in 255 bins (d = M - x / |T| through a
+// reciprocal; deeper values and their 16-byte groups skipped) and collects
+// them as keys; the first bin where the count reaches k bounds the top-k (a
+// window with fewer values is widened, twice as wide, up to 32 nats).  If the
+// window holds more than kWideCap values, one more pass collects the bins up
+// to that one (and the next, when they fit).  The keys are sorted; when the
+// run of values tied with the k-th ends inside them, the finalise keeps the
+// top-k with ties and applies top-p over them (reference sampler.py:116-131).
+// Returns false (the same on every thread) when the row continues on the
+// multi-pass path.
+// ---------------------------------------------------------------------------
+template <int DT>
+__device__ bool wide_topk(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t policy, int k, float topp) {
+  Misc* m = c.m;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float M = m->nuc_M;
+  if (!(M > -INFINITY && M < INFINITY)) return false;  // the candidates did not give it
+  const float r = __frcp_rn(c.Tabs);
+  uint32_t* h = m->hist;
+  uint64_t* keys = reinterpret_cast<uint64_t*>(c.cx);
+  auto key_of = [&](float x, int col) {
+    const float y = __fdiv_rn(x, c.Tabs) + 0.0f;  // -0 and +0 tie
+    return (uint64_t(f2key(y)) << 32) | uint64_t(~uint32_t(c.c0 + col));
+  };
+  float D = fminf(__fsub_rn(M, m->nuc_yk) + 4.0f, kWideMaxNats);  // unknown scale: the widest
+  float S = 0.0f;
+  int jk = INT_MAX, nk = 0, n = 0;
+  for (int att = 0; att < 4; ++att) {
+    S = float(kWideBins - 1) / D;
+    h[tid] = 0u;
+    if (tid == 0) {
+      m->w_bin = INT_MAX;
+      m->w_n = 0;
+    }
+    __syncthreads();
+    warp_pass(
+        c, seq, 0, policy, c.rep, c.pres, c.freq,
+        [&](float x, int col) {
+          if (x > -INFINITY) {
+            const int b = wide_bin(x, M, r, S);
+            if (b < kWideBins - 1) {
+              atomicAdd(&h[b], 1u);
+              const int i = atomicAdd(&m->w_n, 1);
+              if (i < kWideCap) keys[i] = key_of(x, col);
+            }
+          }
+        },
+        [&](int) {}, wide_floor(M, D, c.Tabs));
+    __syncthreads();
+    if (m->flags & F_TIMEOUT) {  // every warp waited for its copies in flight
+      if (tid == 0) a.out_ids[c.row] = NS_ERR_DEVICE_TIMEOUT;
+      return true;
+    }
+    n = m->w_n;
+    // the first bin where the count reaches k
+    const int cnt = (tid < kWideBins - 1) ? int(h[tid]) : 0;
+    int ic = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(kFull, ic, o);
+      if (lane >= o) ic += v;
+    }
+    if (lane == 31) m->i_red[warp] = ic;
+    __syncthreads();
+    for (int w = 0; w < warp; ++w) ic += m->i_red[w];  // never reads the last warp's entry
+    if (ic >= k && ic - cnt < k) {  // one thread at most
+      m->w_bin = tid;
+      m->i_red[kWarps - 1] = ic;
+    }
+    __syncthreads();
+    jk = m->w_bin;
+    nk = (jk != INT_MAX) ? m->i_red[kWarps - 1] : 0;
+    __syncthreads();
+    if (jk != INT_MAX || D >= kWideMaxNats) break;
+    D = fminf(2.0f * D, kWideMaxNats);
+  }
+  if (jk == INT_MAX || nk > kWideCap) return false;
+  if (n > kWideCap) {  // more values than keys: the bins up to jk (and the next if they fit)
+    const int jp = (jk + 1 < kWideBins - 1 && nk + int(h[jk + 1]) <= kWideCap) ? jk + 1 : jk;
+    if (tid == 0) m->w_n = 0;
+    __syncthreads();
+    warp_pass(
+        c, seq, 0, policy, c.rep, c.pres, c.freq,
+        [&](float x, int col) {
+          if (x > -INFINITY && wide_bin(x, M, r, S) <= jp) {
+            const int i = atomicAdd(&m->w_n, 1);
+            if (i < kWideCap) keys[i] = key_of(x, col);
+          }
+        },
+        [&](int) {}, wide_floor(M, float(jp + 1) / S, c.Tabs));
+    __syncthreads();
+    if (m->flags & F_TIMEOUT) {
+      if (tid == 0) a.out_ids[c.row] = NS_ERR_DEVICE_TIMEOUT;
+      return true;
+    }
+    n = m->w_n;
+    if (n > kWideCap || n < k) return false;
+  }
+  uint64_t* tmp = reinterpret_cast<uint64_t*>(c.stages + size_t(kMergeCap) * 8);
+  uint64_t* sorted = reinterpret_cast<uint64_t*>(c.stages + kRankKeysOff) + kRankMax;
+  const float Sb = float(kBins - 1) / D;  // sort buckets: a function of y alone, so ties share one
+  bucket_sort(
+      m, keys, n, tmp, sorted,
+      [&](uint64_t kk) {
+        const float d = (M - key2f(uint32_t(kk >> 32))) * Sb;
+        return d < float(kBins - 1) ? int(fmaxf(d, 0.0f)) : kBins - 1;
+      },
+      [](uint64_t x, uint64_t y) { return x > y; });
+  // the keys are an upper set of x: the run tied with the k-th is complete
+  // when a smaller value follows it among them
+  if (warp == 0) {
+    const int nf = topk_with_ties(sorted, n, k);
+    if (lane == 0) m->w_L = (nf < n) ? nf : -1;
+  }
+  __syncthreads();
+  if (m->w_L < 0) return false;
+  c.K = k;
+  finalize_keys(c, a, c.row, topp, sorted, n, n);
+  return true;
+}
+
 template <int DT>
 __device__ void general_row(const Ctx<DT>& c, const KArgs& a, cg::cluster_group& cl, int CL, int rank, int& seq,
                             int pre_issued, uint64_t policy, float rep, float pres, float freq, float topp) {
@@ -3571,6 +3723,8 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     mode = MODE_GREEDY;
   else if (topk > 0 && int64_t(topk) < a.vocab_total && topk <= kFastK)
     mode = MODE_FAST;
+  else if (topk > kFastK && int64_t(topk) < a.vocab_total && topk <= kWideCap && CL == 1 && !a.vp_keys)
+    mode = MODE_WIDEK;
   else if (!(topk > 0 && int64_t(topk) < a.vocab_total) && !a.vp_keys && !(topp > 0.0f && topp < 1.0f))
     mode = MODE_SOFTMAX;
   else if (!(topk > 0 && int64_t(topk) < a.vocab_total) && !a.vp_keys)
@@ -3580,14 +3734,14 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
   // NUCLEUS (top-k off, top-p on): the FAST filter keeps the kNucleusK largest
   // with ties as candidates, and the tile masses give the row's total; when the
   // candidates hold more than p of it the cut lies among them
-  const bool fastlike = (mode == MODE_FAST || mode == MODE_NUCLEUS);
+  const bool fastlike = (mode == MODE_FAST || mode == MODE_NUCLEUS || mode == MODE_WIDEK);
   if (a.vp_keys && mode == MODE_GENERAL) {  // no candidate record for these rows
     if (rank == 0 && tid == 0) a.out_ids[row] = NS_ERR_UNSUPPORTED;
     return;
   }
   c.neg = T < 0.0f;
   c.Tabs = fabsf(T);
-  c.K = (mode == MODE_NUCLEUS) ? kNucleusK : topk;
+  c.K = (mode == MODE_NUCLEUS || mode == MODE_WIDEK) ? kNucleusK : topk;
   int64_t h0 = 0, h1 = 0;
   if (a.hist_offsets) {
     h0 = a.hist_offsets[row];
@@ -3817,6 +3971,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     if (row_tail(c, a, cluster, CL, rank, mode, ok, s, best, bidx, topp)) return;
     __syncthreads();  // the row continues below
     if (mode == MODE_NUCLEUS && CL == 1 && nucleus_wide(c, a, seq_next, policy, topp)) return;
+    if (mode == MODE_WIDEK && wide_topk(c, a, seq_next, policy, topk, topp)) return;
   }
   if (fastlike) {  // every warp's final bound; survivors of the tightest
     if (ok) publish_bound(c, s);

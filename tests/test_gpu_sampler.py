@@ -266,6 +266,34 @@ def test_nucleus_rows_top_k_off(sampler, dtype, B):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_wide_top_k_rows(sampler, dtype):
+    """Top-k between 241 and 2048 (one block per row): the stream keeps the 240
+    largest, one more pass counts and collects a window below the row's
+    maximum, and the finalise keeps the top-k with ties; a plateau of equal
+    values at the k-th, a plateau above it, negative temperatures and
+    penalised history columns in the window."""
+    B, V = 160, 151936
+    x = make_logits(101, B, V, 3.0, dtype=torch.float32)
+    top = x.max(dim=1).values
+    x[4, 7::211] = top[4] - 1.0                   # ~720 equal values near the top
+    x[9, 3::97] = top[9] - 2.5                    # ~1566 equal values around the k-th
+    x = x.to(dtype)
+    hs = make_histories(102, B, V, 400)
+    rng = np.random.default_rng(103)
+    params = []
+    for b in range(B):
+        pen = dict(repetition_penalty=1.1, presence_penalty=0.3, frequency_penalty=0.1) if b % 2 else {}
+        params.append(SamplingParams(temperature=float(rng.choice([0.5, 0.7, 1.0, -0.8, 1.3])),
+                                     top_k=int(rng.choice([241, 300, 500, 1000, 1500, 2048])),
+                                     top_p=float(rng.choice([1.0, 0.9, 0.5, 0.99])), **pen))
+    params[4] = SamplingParams(temperature=1.0, top_k=300, top_p=1.0)
+    params[9] = SamplingParams(temperature=1.0, top_k=1000, top_p=0.95)
+    u = make_uniforms(104, B)
+    ids, ref = run(sampler, x, hs, params, u)
+    assert check(ids, ref, f"wide top-k {dtype}") <= 6
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_wide_nucleus_rows(sampler, dtype):
     """Top-p only, nuclei of a few hundred to a few thousand values (one block
     per row): the bin-count pass and the key pass, with ties straddling the
