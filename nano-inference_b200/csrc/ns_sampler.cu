@@ -29,7 +29,7 @@
 //       and the draw run on them; otherwise (one CTA per row) one more pass
 //       collects a window of values below the row's maximum (nucleus_wide),
 //       else GENERAL.
-//   WIDEK  (kFastK < top_k <= kWideCap, one CTA per row)
+//   WIDEK  (kWideKFrom <= top_k <= kWideCap, one CTA per row)
 //       FAST with kNucleusK candidates, then one more pass counting and
 //       collecting the values in a window below the row's maximum
 //       (wide_topk), else GENERAL.
@@ -80,6 +80,8 @@ constexpr int kStageBytes = kWarps * kWStages * kWStageStride;
 constexpr int kCapW = 256;                      // per-warp candidate buffer (entries)
 constexpr int kPerLane = kCapW / 32;
 constexpr int kFastK = 240;                     // largest top_k served by the single-pass path
+constexpr int kWideKFrom = 225;                 // one-CTA rows from this top_k on take WIDEK: near kFastK
+                                                // the warps' candidate buffers overflow on some rows
 constexpr int kNucleusK = 128;                  // NUCLEUS candidates (the largest values with ties)
 static_assert((kFastK + kWarps - 1) / kWarps <= 32, "a warp's published rank is one of its 32 lane maxima");
 constexpr int kCandBytes = kWarps * kCapW * 8;  // candidate buffers (x, col)
@@ -3148,7 +3150,7 @@ __device__ bool nucleus_wide(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t poli
 }
 
 // ---------------------------------------------------------------------------
-// Rows with kFastK < top_k <= kWideCap (one CTA per row).  The stream kept
+// Rows with kWideKFrom <= top_k <= kWideCap (one CTA per row).  The stream kept
 // the kNucleusK largest values (with ties): the first is the row's largest
 // scaled value M, the last sets the window scale dk.  One more pass counts the
 // values within D = dk + 4 nats of M in 255 bins (d = M - x / |T| through a
@@ -3721,10 +3723,10 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
   int mode;
   if (T == 0.0f)
     mode = MODE_GREEDY;
+  else if (topk >= kWideKFrom && int64_t(topk) < a.vocab_total && topk <= kWideCap && CL == 1 && !a.vp_keys)
+    mode = MODE_WIDEK;
   else if (topk > 0 && int64_t(topk) < a.vocab_total && topk <= kFastK)
     mode = MODE_FAST;
-  else if (topk > kFastK && int64_t(topk) < a.vocab_total && topk <= kWideCap && CL == 1 && !a.vp_keys)
-    mode = MODE_WIDEK;
   else if (!(topk > 0 && int64_t(topk) < a.vocab_total) && !a.vp_keys && !(topp > 0.0f && topp < 1.0f))
     mode = MODE_SOFTMAX;
   else if (!(topk > 0 && int64_t(topk) < a.vocab_total) && !a.vp_keys)
