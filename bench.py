@@ -44,7 +44,7 @@ GRAPH_LAUNCHES = 500
 # DRAM bytes (read + write) of one headline launch of the sampling kernel,
 # from the ncu capture summarised in profiles/sample_kernel_headline_B256.md
 # (dram__bytes_read.sum + dram__bytes_write.sum of one launch, same workload).
-NCU_TRAFFIC_BYTES = 156777984 + 3761152
+NCU_TRAFFIC_BYTES = 156778752 + 6206464
 
 
 def _peaks():
