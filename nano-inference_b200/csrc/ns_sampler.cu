@@ -2703,10 +2703,11 @@ __device__ __forceinline__ float wide_floor(float M, float dd, float Tabs) {
   return b - (fabsf(M) + dd) * Tabs * 0x1p-18f - 1e-30f;
 }
 
-// Whether every x (the pass's domain) with rn(x / Tabs) == y falls in bin jb:
-// walks the float grid from y * Tabs to the ends of y's class; false (unsure)
-// when a walk takes more than 64 steps or y has no such x.
-__device__ bool y_class_in_bin(float y, float Tabs, float M, float r, float S, int jb) {
+// The bins of the ends of y's class -- every x (the pass's domain) with
+// rn(x / Tabs) == y -- found by walking the float grid from y * Tabs: *blo
+// for its largest x, *bhi for its smallest.  False (unsure) when a walk takes
+// more than 64 steps or y has no such x.
+__device__ bool y_class_bins(float y, float Tabs, float M, float r, float S, int* blo, int* bhi) {
   auto yq = [&](float x) { return __fdiv_rn(x, Tabs) + 0.0f; };
   float x = y * Tabs;
   for (int i = 0; i < 64 && yq(x) < y; ++i) x = nextafterf(x, INFINITY);
@@ -2726,7 +2727,15 @@ __device__ bool y_class_in_bin(float y, float Tabs, float M, float r, float S, i
     hi = nx;
   }
   if (i == 64) return false;
-  return wide_bin(lo, M, r, S) == jb && wide_bin(hi, M, r, S) == jb;
+  *blo = wide_bin(hi, M, r, S);
+  *bhi = wide_bin(lo, M, r, S);
+  return true;
+}
+
+// Whether every x with rn(x / Tabs) == y falls in bin jb.
+__device__ bool y_class_in_bin(float y, float Tabs, float M, float r, float S, int jb) {
+  int blo = 0, bhi = 0;
+  return y_class_bins(y, Tabs, M, r, S, &blo, &bhi) && blo == jb && bhi == jb;
 }
 
 // NUCLEUS rows whose nucleus holds more values than the keys fit (one CTA):
@@ -3230,8 +3239,10 @@ __device__ bool wide_topk(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t policy,
     D = fminf(2.0f * D, kWideMaxNats);
   }
   if (jk == INT_MAX || nk > kWideCap) return false;
+  int jc = kWideBins - 2;  // the last bin the keys hold
   if (n > kWideCap) {  // more values than keys: the bins up to jk (and the next if they fit)
     const int jp = (jk + 1 < kWideBins - 1 && nk + int(h[jk + 1]) <= kWideCap) ? jk + 1 : jk;
+    jc = jp;
     if (tid == 0) m->w_n = 0;
     __syncthreads();
     warp_pass(
@@ -3262,10 +3273,16 @@ __device__ bool wide_topk(Ctx<DT>& c, const KArgs& a, int& seq, uint64_t policy,
       },
       [](uint64_t x, uint64_t y) { return x > y; });
   // the keys are an upper set of x: the run tied with the k-th is complete
-  // when a smaller value follows it among them
+  // when a smaller value follows it among them, or when its whole float
+  // class lies in the bins the keys hold
   if (warp == 0) {
     const int nf = topk_with_ties(sorted, n, k);
-    if (lane == 0) m->w_L = (nf < n) ? nf : -1;
+    if (lane == 0) {
+      int blo = 0, bhi = 0;
+      const bool whole = nf < n || (y_class_bins(key2f(uint32_t(sorted[n - 1] >> 32)), c.Tabs, M, r, S, &blo, &bhi) &&
+                                    bhi <= jc);
+      m->w_L = whole ? nf : -1;
+    }
   }
   __syncthreads();
   if (m->w_L < 0) return false;
