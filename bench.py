@@ -372,6 +372,8 @@ def run_vp(args, world, rank, local):
     assert lib.ns_vp_record_int64s(B, cap, ctypes.byref(n)) == 0
     rec = torch.empty(n.value, dtype=torch.int64, device=dev)
     out = torch.empty(B, dtype=torch.int64, device=dev)
+    vp_ws_bytes = _lib.workspace_bytes(B, width, 0)
+    vp_ws = torch.empty(vp_ws_bytes, dtype=torch.uint8, device=dev)
     side = torch.cuda.Stream(dev)
     peer = args.vp_transport == "peer"
     if peer:
@@ -385,7 +387,8 @@ def run_vp(args, world, rank, local):
         x = bufs[i % N_BUFFERS]
         rp = ex.record(rank, i & 1) if peer else rec.data_ptr()
         rc = lib.ns_vp_local(x.data_ptr(), _lib.NS_DTYPE_F32, B, width, width, off, V, None, None, 0,
-                             pp, pp + 4 * B, pp + 8 * B, None, None, None, cap, rp, side.cuda_stream)
+                             pp, pp + 4 * B, pp + 8 * B, None, None, None, cap, rp,
+                             vp_ws.data_ptr(), vp_ws_bytes, side.cuda_stream)
         assert rc == 0
         if peer:
             rc = lib.ns_vp_signal(flags_arg, world, rank, ex.counter(), side.cuda_stream)

@@ -17,7 +17,13 @@
  *     output: out_ids[b] < 0 is the (negative) ns_status of row b.
  *   - The sampler never writes the logits (the reference mutates them in place
  *     at sampler.py:52; no caller depends on it).
- *   - Kernels are re-entrant and keep no state between calls.
+ *   - ns_sample and ns_vp_local take a caller-allocated device workspace of
+ *     ns_sampler_workspace_bytes bytes (256-byte aligned; 0 bytes, and NULL
+ *     allowed, when max_history <= 1024).  It holds the history rank arrays
+ *     of blocks that meet more distinct history ids than their shared memory
+ *     keeps, so shared memory does not grow with the history length.  A call
+ *     needs no particular contents on entry and leaves nothing the next call
+ *     reads, but two calls that overlap on the device must not share one.
  */
 #ifndef NS_SAMPLER_H
 #define NS_SAMPLER_H
@@ -62,7 +68,14 @@ const char* ns_status_string(int status);
 int ns_version(void);
 
 /*
- * Scratch bytes ns_sample needs for this problem size (may be 0).
+ * Workspace bytes ns_sample / ns_vp_local need for this problem size
+ * (vocab: the columns the call reads).  0 when max_history <= 1024 (a
+ * block's distinct history ids fit its shared memory); otherwise 12 B per
+ * block per min(max_history, columns of a block): batch x (1-8 blocks per
+ * row, by batch, vocab and the current device's SM count) blocks; 100.7 MB at
+ * batch 256, vocab 151936, max_history 32768 on a 148-SM device.  Without a
+ * device the widest clusters the vocabulary allows are assumed (an upper
+ * bound).
  * Replaces: nothing (the reference allocates per call inside torch ops).
  */
 int ns_sampler_workspace_bytes(int64_t batch, int64_t vocab, int64_t max_history,
@@ -91,6 +104,9 @@ int ns_sampler_workspace_bytes(int64_t batch, int64_t vocab, int64_t max_history
  *               draws Philox4x32-10(counter = (row, philox_offset),
  *               key = philox_seed).
  * out_ids       int64 [batch]: sampled token id, or a negative ns_status.
+ * workspace     device scratch of at least ns_sampler_workspace_bytes(batch,
+ *               vocab, max_history) bytes, 256-byte aligned; otherwise the
+ *               call returns NS_ERR_WORKSPACE_TOO_SMALL.
  */
 int ns_sample(const void* logits, int dtype, int64_t batch, int64_t vocab, int64_t row_stride,
               const int32_t* hist_ids, const int64_t* hist_offsets, int64_t max_history,
@@ -120,14 +136,17 @@ int ns_vp_record_int64s(int64_t batch, int cap, int64_t* out_count);
  * slice penalises the ones it holds.  Writes per row the top-k survivors
  * (ties at the k-th value kept) as keys, or for greedy rows (T == 0) one key.
  * Rows with top-k off or k > 240 report NS_ERR_UNSUPPORTED; more than `cap`
- * survivors report NS_ERR_CANDIDATE_OVERFLOW.  cap in [1, 1024].
+ * survivors report NS_ERR_CANDIDATE_OVERFLOW.  cap in [1, 1024].  workspace:
+ * ns_sampler_workspace_bytes(batch, vocab_local, max_history) bytes, as in
+ * ns_sample.
  */
 int ns_vp_local(const void* logits, int dtype, int64_t batch, int64_t vocab_local, int64_t row_stride,
                 int64_t vocab_offset, int64_t vocab_total,
                 const int32_t* hist_ids, const int64_t* hist_offsets, int64_t max_history,
                 const float* temperature, const int32_t* top_k, const float* top_p,
                 const float* repetition_penalty, const float* presence_penalty,
-                const float* frequency_penalty, int cap, int64_t* record, ns_stream_t stream);
+                const float* frequency_penalty, int cap, int64_t* record,
+                void* workspace, size_t workspace_bytes, ns_stream_t stream);
 
 /*
  * Merge the all-gathered records (n_ranks consecutive records, rank order)

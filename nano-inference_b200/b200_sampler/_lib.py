@@ -55,7 +55,7 @@ PROTOTYPES = {
         _c_vp, _c_vp, _c_i64,                        # hist_ids, hist_offsets, max_history
         _c_vp, _c_vp, _c_vp,                         # temperature, top_k, top_p
         _c_vp, _c_vp, _c_vp,                         # repetition, presence, frequency
-        _c_int, _c_vp, _c_vp,                        # cap, record, stream
+        _c_int, _c_vp, _c_vp, _c_sz, _c_vp,          # cap, record, workspace, workspace_bytes, stream
     ]),
     "ns_vp_merge": (_c_int, [
         _c_vp, _c_int, _c_i64, _c_int, _c_i64,       # gathered, n_ranks, batch, cap, vocab_total
@@ -104,3 +104,12 @@ def load() -> ctypes.CDLL:
 
 def status_string(code: int) -> str:
     return load().ns_status_string(int(code)).decode()
+
+
+def workspace_bytes(batch: int, vocab: int, max_history: int) -> int:
+    """Device workspace (bytes) an ns_sample / ns_vp_local call of this size needs."""
+    n = ctypes.c_size_t()
+    rc = load().ns_sampler_workspace_bytes(int(batch), int(vocab), int(max_history), ctypes.byref(n))
+    if rc != NS_OK:
+        raise ValueError(f"ns_sampler_workspace_bytes: {status_string(rc)}")
+    return int(n.value)

@@ -33,6 +33,7 @@ import torch
 
 from . import _lib
 from .params import pack_params
+from .workspace import Workspace
 
 try:  # C-level history packing (built with the library); array.array otherwise
     from ._histpack import pack as _pack_histories
@@ -130,6 +131,7 @@ class B200Sampler(SamplerBase):
         self.seed = int(seed) & 0xFFFFFFFFFFFFFFFF
         self.offset = 0
         self._staging = {}
+        self._workspace = {}  # device index -> Workspace
         self._landing = {}   # device index -> (device buffer for host logits, event after its last reader)
         self._lock = threading.Lock()
 
@@ -184,13 +186,18 @@ class B200Sampler(SamplerBase):
             st = self._stage(device, B, all_generated_ids, all_sampling_params, uniforms, stream)
             offset = self.offset
             self.offset += 1
+            ws = self._workspace.get(device.index)
+            if ws is None:
+                ws = self._workspace[device.index] = Workspace(device)
+            ws_ptr, ws_bytes = ws.acquire(B, V, st.max_hist if st.hist_ids is not None else 0, stream)
             rc = self.lib.ns_sample(
                 logits.data_ptr(), _DTYPES[logits.dtype], B, V, int(logits.stride(0)),
                 st.hist_ids, st.hist_offsets, st.max_hist,
                 st.p32, st.p32 + 4 * B, st.p32 + 8 * B,
                 st.p32 + 12 * B, st.p32 + 16 * B, st.p32 + 20 * B,
                 st.u_ptr, self.seed, offset,
-                out.data_ptr(), None, 0, stream.cuda_stream)
+                out.data_ptr(), ws_ptr, ws_bytes, stream.cuda_stream)
+            ws.release(stream)
             st.keep_alive(stream)
             if landed is not None:
                 landed.record(stream)   # the next call's copy waits for this launch
@@ -303,7 +310,9 @@ class DeviceBatch:
     for repeated launches on logits that change every step -- the shape of a
     decode loop whose histories live on the GPU.  ``launch`` is one
     ``ns_sample`` call with no host work, so it can be captured in a CUDA
-    graph."""
+    graph (after a first launch outside the capture has allocated the
+    workspace).  The batch owns its workspace: launches of one DeviceBatch
+    must not overlap on the device."""
 
     def __init__(self, histories: Optional[Sequence[Sequence[int]]], params, device,
                  uniforms: Optional[torch.Tensor] = None, seed: int = 0):
@@ -325,8 +334,10 @@ class DeviceBatch:
             self.hist_ids = self.hist_offsets = None
             self.max_history = 0
         self.uniforms = None if uniforms is None else uniforms.to(self.device, torch.float32).contiguous()
+        self.workspace = Workspace(self.device)
 
     def nbytes(self) -> int:
+        """Bytes of the per-row inputs (params, history CSR, uniforms)."""
         n = self.params.numel() * 4
         if self.hist_ids is not None:
             n += self.hist_ids.numel() * 4 + self.hist_offsets.numel() * 8
@@ -340,10 +351,11 @@ class DeviceBatch:
         assert B == self.batch and logits.stride(1) == 1 and out.numel() >= B
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
         p = self.params.data_ptr()
+        ws_ptr, ws_bytes = self.workspace.acquire(B, V, self.max_history if self.hist_ids is not None else 0)
         return self.lib.ns_sample(
             logits.data_ptr(), _DTYPES[logits.dtype], B, V, int(logits.stride(0)),
             None if self.hist_ids is None else self.hist_ids.data_ptr(),
             None if self.hist_offsets is None else self.hist_offsets.data_ptr(),
             self.max_history, p, p + 4 * B, p + 8 * B, p + 12 * B, p + 16 * B, p + 20 * B,
             None if self.uniforms is None else self.uniforms.data_ptr(), self.seed, offset,
-            out.data_ptr(), None, 0, s.cuda_stream)
+            out.data_ptr(), ws_ptr, ws_bytes, s.cuda_stream)

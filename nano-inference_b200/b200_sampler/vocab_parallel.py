@@ -36,6 +36,7 @@ import torch.distributed as dist
 from . import _lib
 from .params import pack_params
 from .sampler import _DTYPES, _ROW_ERRORS, B200Sampler
+from .workspace import Workspace
 
 FAST_MAX_K = 240       # largest top_k the candidate records serve (kFastK in the kernel)
 MAX_CAP = 1024         # record capacity limit (kRankMax in the kernel)
@@ -252,12 +253,17 @@ class VocabParallelSampler(B200Sampler):
             if offset is None:
                 offset = self.offset
                 self.offset += 1
+            ws = self._workspace.get(device.index)
+            if ws is None:
+                ws = self._workspace[device.index] = Workspace(device)
+            ws_ptr, ws_bytes = ws.acquire(B, self.vocab_local, st.max_hist if st.hist_ids is not None else 0, stream)
             rc = self.lib.ns_vp_local(
                 logits.data_ptr(), _DTYPES[logits.dtype], B, self.vocab_local, int(logits.stride(0)),
                 self.vocab_offset, self.vocab_total,
                 st.hist_ids, st.hist_offsets, st.max_hist,
                 st.p32, st.p32 + 4 * B, st.p32 + 8 * B, st.p32 + 12 * B, st.p32 + 16 * B, st.p32 + 20 * B,
-                cap, rec_ptr, stream.cuda_stream)
+                cap, rec_ptr, ws_ptr, ws_bytes, stream.cuda_stream)
+            ws.release(stream)
             if rc != _lib.NS_OK:
                 raise RuntimeError(f"ns_vp_local failed: {_lib.status_string(rc)}")
             if peer:

@@ -92,6 +92,11 @@ constexpr int kMaxCluster = 8;
 constexpr int kMergeCap = 4096;
 static_assert(kMergeCap * 16 <= kStageBytes, "merge lists and their sort keys fit the stage area");
 constexpr int kMaxLists = kMaxCluster * kWarps;
+// Distinct history ids one CTA keeps in shared memory (12 B each: count,
+// column, penalised value).  A CTA whose columns hold more moves its rank
+// arrays to the caller's workspace, so shared memory does not grow with the
+// history length.
+constexpr int kHistSmem = 1024;
 constexpr unsigned kFull = 0xFFFFFFFFu;
 
 enum : int { MODE_GREEDY = 0, MODE_FAST = 1, MODE_GENERAL = 2, MODE_SOFTMAX = 3, MODE_NUCLEUS = 4, MODE_WIDEK = 5 };
@@ -154,6 +159,7 @@ struct Misc {
   double s_rem;             // SOFTMAX: the draw's remaining mass inside the chosen warp
   int s_warp;               // ... and that warp
   int s_rank;               // ... and that CTA of the cluster
+  int hist_g;               // the rank arrays live in the workspace (more than cnt_cap distinct ids)
   float c_M;                // SOFTMAX clusters: this CTA's largest scaled value
   double c_W;               // ... and its mass with the row's largest
   float nuc_M;              // NUCLEUS: the row's largest scaled value
@@ -195,7 +201,13 @@ struct KArgs {
   int per_warp;    // columns per warp (multiple of the 16-byte vector width)
   int tpw;         // tiles per warp (upper bound)
   int nwords;      // history bitmap words (one bit per column of a CTA)
-  int cnt_cap;     // distinct history ids the rank arrays hold
+  int cnt_cap;     // distinct history ids the shared-memory rank arrays hold
+  // rank arrays of CTAs with more distinct ids (nullptr: none): per CTA
+  // hist_ws_cap counts, then columns, then penalised values
+  int32_t* hist_ws;
+  int hist_ws_cap;
+  void* ws;         // the caller's workspace and its size
+  size_t ws_bytes;
   int merge_cap;   // leader merge area (entries)
   // vocab-parallel local step: out_ids[] receives each row's survivor count
   // (or a negative status) and vp_keys[row * vp_cap ...] its sorted keys
@@ -3800,6 +3812,7 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
     m->choose = INT_MAX;
     m->g_best = -INFINITY;
     m->g_idx = INT_MAX;
+    m->hist_g = 0;
     for (int w = 0; w < kWarps; ++w) m->pub[w] = 0u;
   }
   if (pen) {
@@ -3897,9 +3910,24 @@ __global__ void __launch_bounds__(kThreads, 2) sample_kernel(const __grid_consta
         wide |= m->i_red[w] > 0xFFFF;  // the 16-bit prefixes would wrap
       }
       m->segoff[kWarps] = acc;
-      if (acc > a.cnt_cap || wide) atomicOr(&m->flags, F_HIST);
+      if (wide) {
+        atomicOr(&m->flags, F_HIST);
+      } else if (acc > a.cnt_cap) {
+        if (a.hist_ws && acc <= a.hist_ws_cap)
+          m->hist_g = 1;
+        else
+          atomicOr(&m->flags, F_HIST);
+      }
     }
     __syncthreads();
+    if (m->hist_g && !(m->flags & F_HIST)) {  // this CTA's rank arrays in its workspace slot
+      int32_t* base = a.hist_ws + size_t(blockIdx.x) * 3 * size_t(a.hist_ws_cap);
+      c.cnt = base;
+      c.colr = base + a.hist_ws_cap;
+      c.pval = reinterpret_cast<float*>(base + 2 * size_t(a.hist_ws_cap));
+      for (int i = tid; i < m->segoff[kWarps]; i += kThreads) c.cnt[i] = 0;
+      __syncthreads();
+    }
     if (!(m->flags & F_HIST)) {
       const int wpw = c.pw >> 5;
       auto count = [&](int rel) {
@@ -4306,38 +4334,80 @@ struct DeviceInfo {
 static std::mutex g_mu;
 static DeviceInfo g_dev[64];
 
-template <int DT>
-static int launch(const KArgs& base, int64_t batch, ns_stream_t stream) {
-  using C_ = Ctx<DT>;
+static int device_info(DeviceInfo** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return NS_ERR_CUDA;
   DeviceInfo* di = &g_dev[dev];
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (di->sms == 0) {
-      if (cudaDeviceGetAttribute(&di->sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-        return NS_ERR_CUDA;
-      if (cudaDeviceGetAttribute(&di->max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) !=
-          cudaSuccess)
-        return NS_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (di->sms == 0) {
+    int sms = 0, optin = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return NS_ERR_CUDA;
+    if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+      return NS_ERR_CUDA;
+    di->max_smem_optin = optin;
+    di->sms = sms;
+  }
+  *out = di;
+  return NS_OK;
+}
+
+// Launch shape of a call: CTAs per row (a cluster) and the columns of a CTA
+// and of a warp.
+struct Geom {
+  int CL;
+  int64_t per, pw, span;
+};
+
+template <int DT>
+static Geom geometry(int64_t batch, int64_t V, int sms) {
+  using C_ = Ctx<DT>;
+  Geom g;
+  // CTAs per row: enough rows x CTAs to cover the SMs, each warp >= 1 tile.
+  g.CL = 1;
+  while (g.CL < kMaxCluster && batch * g.CL < sms && V / (2 * g.CL) >= int64_t(kWarps) * C_::TE) g.CL *= 2;
+  g.per = (V + g.CL - 1) / g.CL;
+  g.per = (g.per + C_::VE - 1) / C_::VE * C_::VE;
+  g.pw = (g.per + kWarps - 1) / kWarps;
+  g.pw = (g.pw + 127) / 128 * 128;  // warp ranges start on 16-byte groups of bitmap words
+  g.span = int64_t(kWarps) * g.pw;  // columns one CTA may own
+  return g;
+}
+
+// Distinct history ids a CTA may meet, and the workspace bytes for the rank
+// arrays of every CTA when that is more than shared memory holds (else 0).
+static int64_t hist_cap(int64_t max_history, const Geom& g) {
+  return std::min<int64_t>(std::max<int64_t>(max_history, 1), g.span);
+}
+static size_t hist_ws_need(int64_t batch, int64_t max_history, const Geom& g) {
+  const int64_t cap = hist_cap(max_history, g);
+  return cap > kHistSmem ? size_t(batch) * size_t(g.CL) * 12 * size_t(cap) : 0;
+}
+
+template <int DT>
+static int launch(const KArgs& base, int64_t batch, ns_stream_t stream) {
+  using C_ = Ctx<DT>;
+  DeviceInfo* di = nullptr;
+  if (const int rc = device_info(&di)) return rc;
+  KArgs a = base;
+  const Geom g = geometry<DT>(batch, a.vocab, di->sms);
+  const int CL = g.CL;
+  a.per_cta = int(g.per);
+  a.per_warp = int(g.pw);
+  a.tpw = int((g.pw + C_::TE - 1) / C_::TE);
+  const int n_tiles_all = kWarps * a.tpw;
+  a.nwords = a.hist_ids ? int((g.span + 31) / 32) : 0;
+  a.cnt_cap = a.hist_ids ? int(std::min<int64_t>(hist_cap(a.max_history, g), kHistSmem)) : 0;
+  a.hist_ws = nullptr;
+  a.hist_ws_cap = 0;
+  if (a.hist_ids) {
+    const size_t need = hist_ws_need(batch, a.max_history, g);
+    if (need > 0) {
+      if (!a.ws || a.ws_bytes < need || (reinterpret_cast<uintptr_t>(a.ws) & 255u) != 0)
+        return NS_ERR_WORKSPACE_TOO_SMALL;
+      a.hist_ws = static_cast<int32_t*>(a.ws);
+      a.hist_ws_cap = int(hist_cap(a.max_history, g));
     }
   }
-  KArgs a = base;
-  const int64_t V = a.vocab;
-  // CTAs per row: enough rows x CTAs to cover the SMs, each warp >= 1 tile.
-  int CL = 1;
-  while (CL < kMaxCluster && batch * CL < di->sms && V / (2 * CL) >= int64_t(kWarps) * C_::TE) CL *= 2;
-  int64_t per = (V + CL - 1) / CL;
-  per = (per + C_::VE - 1) / C_::VE * C_::VE;
-  int64_t pw = (per + kWarps - 1) / kWarps;
-  pw = (pw + 127) / 128 * 128;  // warp ranges start on 16-byte groups of bitmap words
-  a.per_cta = int(per);
-  a.per_warp = int(pw);
-  a.tpw = int((pw + C_::TE - 1) / C_::TE);
-  const int n_tiles_all = kWarps * a.tpw;
-  const int64_t span = int64_t(kWarps) * pw;  // columns one CTA may own
-  a.nwords = a.hist_ids ? int((span + 31) / 32) : 0;
-  a.cnt_cap = a.hist_ids ? int(std::min<int64_t>(std::max<int64_t>(a.max_history, 1), span)) : 0;
   const Layout L = make_layout(a.nwords, a.cnt_cap, n_tiles_all);
   a.merge_cap = kMergeCap;
   a.off_bar = L.off_bar;
@@ -4424,7 +4494,18 @@ int ns_version(void) { return 100; }
 
 int ns_sampler_workspace_bytes(int64_t batch, int64_t vocab, int64_t max_history, size_t* out_bytes) {
   if (!out_bytes || batch < 0 || vocab <= 0 || max_history < 0) return NS_ERR_INVALID_ARGUMENT;
+  if (vocab > (int64_t(1) << 24) || batch > (int64_t(1) << 24)) return NS_ERR_INVALID_ARGUMENT;
   *out_bytes = 0;
+  if (max_history <= ns::kHistSmem) return NS_OK;
+  // The launch shape depends on the device's SM count; without a device the
+  // widest clusters the vocabulary allows bound it (the bytes never shrink
+  // as clusters widen).
+  ns::DeviceInfo* di = nullptr;
+  const int sms = ns::device_info(&di) == NS_OK ? di->sms : INT_MAX;
+  if (!di) (void)cudaGetLastError();
+  const size_t f32 = ns::hist_ws_need(batch, max_history, ns::geometry<NS_DTYPE_F32>(batch, vocab, sms));
+  const size_t b16 = ns::hist_ws_need(batch, max_history, ns::geometry<NS_DTYPE_BF16>(batch, vocab, sms));
+  *out_bytes = std::max(f32, b16);
   return NS_OK;
 }
 
@@ -4434,8 +4515,6 @@ int ns_sample(const void* logits, int dtype, int64_t batch, int64_t vocab, int64
               const float* repetition_penalty, const float* presence_penalty, const float* frequency_penalty,
               const float* uniforms, uint64_t philox_seed, uint64_t philox_offset, int64_t* out_ids,
               void* workspace, size_t workspace_bytes, ns_stream_t stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   if (dtype != NS_DTYPE_F32 && dtype != NS_DTYPE_BF16 && dtype != NS_DTYPE_F16) return NS_ERR_UNSUPPORTED_DTYPE;
   if (batch < 0 || vocab <= 0 || row_stride < vocab || max_history < 0) return NS_ERR_INVALID_ARGUMENT;
   if (vocab > (int64_t(1) << 24) || batch > (int64_t(1) << 24)) return NS_ERR_INVALID_ARGUMENT;
@@ -4461,6 +4540,8 @@ int ns_sample(const void* logits, int dtype, int64_t batch, int64_t vocab, int64
   a.seed = philox_seed;
   a.offset = philox_offset;
   a.out_ids = out_ids;
+  a.ws = workspace;
+  a.ws_bytes = workspace_bytes;
   switch (dtype) {
     case NS_DTYPE_F32: return ns::launch<NS_DTYPE_F32>(a, batch, stream);
     case NS_DTYPE_BF16: return ns::launch<NS_DTYPE_BF16>(a, batch, stream);
@@ -4478,7 +4559,7 @@ int ns_vp_local(const void* logits, int dtype, int64_t batch, int64_t vocab_loca
                 int64_t vocab_offset, int64_t vocab_total, const int32_t* hist_ids, const int64_t* hist_offsets,
                 int64_t max_history, const float* temperature, const int32_t* top_k, const float* top_p,
                 const float* repetition_penalty, const float* presence_penalty, const float* frequency_penalty,
-                int cap, int64_t* record, ns_stream_t stream) {
+                int cap, int64_t* record, void* workspace, size_t workspace_bytes, ns_stream_t stream) {
   if (dtype != NS_DTYPE_F32 && dtype != NS_DTYPE_BF16 && dtype != NS_DTYPE_F16) return NS_ERR_UNSUPPORTED_DTYPE;
   if (batch < 0 || vocab_local <= 0 || row_stride < vocab_local || max_history < 0) return NS_ERR_INVALID_ARGUMENT;
   if (vocab_offset < 0 || vocab_total < vocab_offset + vocab_local || vocab_total > (int64_t(1) << 24) ||
@@ -4506,6 +4587,8 @@ int ns_vp_local(const void* logits, int dtype, int64_t batch, int64_t vocab_loca
   a.out_ids = record;           // [batch] counts / statuses
   a.vp_keys = record + batch;   // [batch][cap] keys
   a.vp_cap = cap;
+  a.ws = workspace;
+  a.ws_bytes = workspace_bytes;
   switch (dtype) {
     case NS_DTYPE_F32: return ns::launch<NS_DTYPE_F32>(a, batch, stream);
     case NS_DTYPE_BF16: return ns::launch<NS_DTYPE_BF16>(a, batch, stream);

@@ -6,6 +6,7 @@ import os
 import re
 
 import pytest
+import torch
 
 from b200_sampler import _lib
 from b200_sampler.build import INCLUDE
@@ -44,8 +45,17 @@ def test_workspace_query():
     lib = _lib.load()
     sz = ctypes.c_size_t(123)
     assert lib.ns_sampler_workspace_bytes(256, 151936, 1024, ctypes.byref(sz)) == 0
-    assert sz.value == 0
+    assert sz.value == 0                     # 1024 distinct ids fit a block's shared memory
+    # longer histories: 12 B per block per min(max_history, columns of a
+    # block).  Without a device the widest clusters the vocabulary allows are
+    # assumed: 8 blocks of 19456 columns per row at vocab 151936.
+    assert lib.ns_sampler_workspace_bytes(256, 151936, 32768, ctypes.byref(sz)) == 0
+    if not torch.cuda.is_available():
+        assert sz.value == 256 * 8 * 12 * 19456
+    assert sz.value >= 256 * 12 * 32768      # at least one block per row
+    assert _lib.workspace_bytes(256, 151936, 1025) > 0
     assert lib.ns_sampler_workspace_bytes(-1, 10, 0, ctypes.byref(sz)) == _lib.NS_ERR_INVALID_ARGUMENT
+    assert lib.ns_sampler_workspace_bytes(1, 1 << 25, 0, ctypes.byref(sz)) == _lib.NS_ERR_INVALID_ARGUMENT
 
 
 def _call(**kw):

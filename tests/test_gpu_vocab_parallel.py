@@ -42,12 +42,14 @@ def vp_sample(x_dev, hs, params, u_dev, bounds, cap):
     assert lib.ns_vp_record_int64s(B, cap, ctypes.byref(n)) == 0
     recs = torch.empty(len(bounds), n.value, dtype=torch.int64, device=dev)
     stream = torch.cuda.current_stream().cuda_stream
+    ws_bytes = max(_lib.workspace_bytes(B, w, hmax) for _, w in bounds)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)   # the slices run one after another
     for r, (off, w) in enumerate(bounds):
         view = x_dev[:, off:off + w]
         rc = lib.ns_vp_local(view.data_ptr(), _DT[x_dev.dtype], B, w, int(view.stride(0)), off, V,
                              hid.data_ptr(), hoff.data_ptr(), hmax,
                              pp, pp + 4 * B, pp + 8 * B, pp + 12 * B, pp + 16 * B, pp + 20 * B,
-                             cap, recs[r].data_ptr(), stream)
+                             cap, recs[r].data_ptr(), ws.data_ptr(), ws_bytes, stream)
         assert rc == 0, _lib.status_string(rc)
     out = torch.empty(B, dtype=torch.int64, device=dev)
     rc = lib.ns_vp_merge(recs.data_ptr(), len(bounds), B, cap, V, pp, pp + 4 * B, pp + 8 * B,
