@@ -1,23 +1,36 @@
 """Benchmark of the B200 token sampler on the north-star headline workload.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload headline|c1|c2|c3|topp095|softmax|k240] [--mode rows|vp]
 
-Workload (per GPU, weak scaling): B=256 rows x V=151936 fp32 logits ``randn*3``,
-T=0.7, top-k 50, top-p 0.9, repetition 1.1, presence 0.5, frequency 0.3, 1024
-uniform history ids per row, one caller uniform per row (synthetic, seeded; the
-reference publishes no benchmark data).
+Headline workload: B=256 rows x V=151936 fp32 logits ``randn*3``, T=0.7,
+top-k 50, top-p 0.9, repetition 1.1, presence 0.5, frequency 0.3, 1024
+uniform history ids per row, one caller uniform per row (synthetic, seeded;
+the reference publishes no benchmark data).  ``--workload`` selects the other
+BASELINE configurations and modes (``b200_sampler.workloads.WORKLOADS``).
 
-One step = one ``ns_sample`` launch over one batch.  ``value`` is sampled
-tokens/s over all ranks with inputs resident in HBM, timed with CUDA events
-around CUDA-graph replays totalling exactly K launches (graphs of up to
-GRAPH_LAUNCHES launches) that rotate over 3 logits buffers (467 MB in total,
-> the 126 MB L2), max over ranks.  ``e2e`` is the same
-metric through the public ``B200Sampler.select_batch`` call with the logits
-in pinned host memory and the histories as Python lists (H2D copies, packing
-and the ids' D2H read inside the timed region).
+One step = one ``ns_sample`` launch over the batch.  With N GPUs the one
+batch is sharded by rows (strong scaling: rank r samples rows
+[r B / N, (r + 1) B / N)); a second, labelled measurement gives every rank the
+full batch (weak scaling).  ``value`` is sampled tokens/s of the whole batch
+with inputs resident in HBM: CUDA-graph replays of exactly K launches that
+rotate over 3 logits buffers (> the 126 MB L2 at the headline), timed with
+CUDA events on the launching stream and bracketed by a barrier and a device
+synchronisation; the K-step region is repeated until >= 1 s has elapsed and
+the median repeat (max over ranks) is reported.  ``e2e`` is the same metric
+through the public ``B200Sampler.select_batch`` call with the logits in pinned
+host memory and the histories as Python lists (H2D copies, packing and the
+ids' D2H read inside the timed region).
 
-``--impl reference`` times the CPU restatement of the reference sampler
-(``oracle/``) on the host cores, on a bounded sample of rows per step.
+``cpu_baseline`` (rank 0, N=1): the reference's own torch
+``Sampler.select_batch`` (installed unmodified under baseline/_ref by
+baseline/install_reference.py), else the numpy restatement in ``oracle/``,
+on a bounded sample of the workload's rows with all host threads.  The same
+leg checks every row of the benchmarked launch against the oracle and fails
+the run on a mismatch.
+
+``--impl reference`` times that reference sampler on the full batch per step
+(all host threads), steps bounded by a ~60 s budget.
 """
 from __future__ import annotations
 
@@ -41,10 +54,16 @@ METRIC = "sampled tokens/sec and logits HBM GB/s vs peak at B=256,V=151936"
 UNIT = "tokens/s"
 N_BUFFERS = 3
 GRAPH_LAUNCHES = 500
-# DRAM bytes (read + write) of one headline launch of the sampling kernel,
-# from the ncu capture summarised in profiles/sample_kernel_headline_B256.md
-# (dram__bytes_read.sum + dram__bytes_write.sum of one launch, same workload).
+MIN_TIMED_S = 1.0
+REF_BUDGET_S = 60.0
+# DRAM bytes (read + write) of one headline launch of the sampling kernel as
+# ncu counted them (dram__bytes_read.sum + dram__bytes_write.sum of one launch
+# of the headline workload, captured with --clock-control none on a B200 of
+# this pool).  A recorded constant, not measured by this script; it describes
+# --workload headline only.
 NCU_TRAFFIC_BYTES = 156778752 + 6206464
+NCU_TRAFFIC_SOURCE = ("recorded constant: ncu dram__bytes_read.sum + dram__bytes_write.sum of one headline "
+                      "launch (sample_kernel<fp32>, B=256), not measured by this run")
 
 
 def _peaks():
@@ -59,6 +78,10 @@ def _peaks():
 def algorithmic_bytes(B: int, V: int, H: int, esz: int = 4) -> int:
     """Logits once + history ids + 36 B/row (6 fp32 params, uniform, int64 id)."""
     return B * V * esz + B * H * 4 + B * 36
+
+
+def metric_for(workload: str) -> str:
+    return METRIC if workload == "headline" else f"sampled tokens/sec and logits HBM GB/s vs peak, workload {workload}"
 
 
 class ClockSampler:
@@ -152,12 +175,52 @@ def max_over_ranks(world, v: float) -> float:
 
 
 # ---------------------------------------------------------------------------
-# CPU arm: the oracle restatement of the reference sampler
+# CPU legs: the reference's own torch sampler, or the numpy restatement
 # ---------------------------------------------------------------------------
-def cpu_port_tokens_per_s(w, rows: int, steps: int = 1, threads: int = 1):
+def reference_sampler():
+    """(Sampler instance, its SamplingParams class, None) from the unmodified
+    reference under baseline/_ref, or (None, None, reason)."""
+    ref = os.path.join(REPO, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "nano_inference")):
+        return None, None, "baseline/_ref holds no reference install (run baseline/install_reference.py)"
+    if ref not in sys.path:
+        sys.path.insert(0, ref)
+    try:
+        from nano_inference.core.sampling import SamplingParams as RefParams
+        from nano_inference.sampling import Sampler
+    except Exception as e:  # pragma: no cover - depends on the install
+        return None, None, f"import failed: {type(e).__name__}: {e}"
+    return Sampler(), RefParams, None
+
+
+def _ref_params(RefParams, params):
+    # the reference's SamplingParams has no presence / frequency penalty
+    # (core/sampling.py); those are dropped in its arm
+    return [RefParams(temperature=float(p.temperature), top_k=int(p.top_k), top_p=float(p.top_p),
+                      repetition_penalty=float(p.repetition_penalty)) for p in params]
+
+
+def cpu_rate(w, rows: int, steps: int, threads: int):
+    """Tokens/s of the reference torch sampler (or the numpy port) over the
+    first `rows` rows of workload `w`, `steps` times; returns (rate, seconds,
+    kind, note).  Each step's select_batch gets a fresh copy of the logits
+    (the reference writes them in place), made outside the timed span."""
+    torch.set_num_threads(threads)
+    sampler, RefParams, why = reference_sampler()
+    if sampler is not None:
+        ps = _ref_params(RefParams, w.params[:rows])
+        hs = w.histories[:rows]
+        src = w.logits[:rows]
+        dt = 0.0
+        for _ in range(steps):
+            x = src.clone()
+            t0 = time.perf_counter()
+            sampler.select_batch(x, hs, ps)
+            dt += time.perf_counter() - t0
+        return rows * steps / dt, dt, "reference", "reference Sampler.select_batch (sampling/sampler.py:36-91)"
     from concurrent.futures import ThreadPoolExecutor
     from oracle import sampler_oracle as O
-    x = w.logits.numpy()
+    x = w.logits.float().numpy()
     u = w.uniforms.numpy()
 
     def one(b):
@@ -165,42 +228,56 @@ def cpu_port_tokens_per_s(w, rows: int, steps: int = 1, threads: int = 1):
 
     t0 = time.perf_counter()
     for _ in range(steps):
-        if threads > 1:
-            with ThreadPoolExecutor(threads) as ex:
-                list(ex.map(one, range(rows)))
-        else:
-            for b in range(rows):
-                one(b)
+        with ThreadPoolExecutor(threads) as ex:
+            list(ex.map(one, range(rows)))
     dt = time.perf_counter() - t0
-    return rows * steps / dt, dt
+    return rows * steps / dt, dt, "port", f"numpy restatement in oracle/ ({why})"
+
+
+def parity_gate(w, ids):
+    """Every row of the benchmarked launch against the oracle: greedy rows
+    bit-exact, sampled rows equal unless the oracle marks them exempt (a
+    top-p cumsum or inverse-CDF step within 1e-6 of its threshold) and the id
+    is one of its alternatives."""
+    from oracle import sampler_oracle as O
+    ref = O.sample_batch(w.logits.float().numpy(), w.histories, w.params, uniforms=w.uniforms.numpy())
+    bad, exempt = [], 0
+    for b, r in enumerate(ref):
+        if r.error:
+            if ids[b] >= 0:
+                bad.append(b)
+        elif ids[b] != r.token:
+            if r.exempt and ids[b] in r.allowed:
+                exempt += 1
+            else:
+                bad.append(b)
+    return {"rows": len(ref), "mismatch": len(bad), "exempt": exempt, "ok": not bad,
+            "first_bad": bad[:8], "oracle": "oracle/sampler_oracle.py"}
 
 
 def run_reference(args, world, rank):
-    """The CPU reference arm: rows of the headline workload through the numpy
-    restatement, all host threads across rows.  A step is one round of
-    `threads` rows; the run stops after the requested steps or a ~90 s budget,
-    whichever comes first, and reports both counts."""
+    """The reference arm: the full batch of the workload through the
+    reference's own torch sampler per step (all host threads), steps bounded
+    by a ~60 s budget.  Rank 0 only."""
     if rank != 0:
         return
-    from b200_sampler.workloads import headline
-    w = headline()
+    from b200_sampler.workloads import WORKLOADS
+    w = WORKLOADS[args.workload]()
     threads = os.cpu_count() or 1
-    rows = min(w.batch, threads)
-    cpu_port_tokens_per_s(w, rows, 1, threads)                      # warm-up round
-    _, t_round = cpu_port_tokens_per_s(w, rows, 1, threads)
-    steps_run = int(max(1, min(args.steps, 90.0 / max(t_round, 1e-6))))
-    for _ in range(min(args.warmup, 1)):
-        cpu_port_tokens_per_s(w, rows, 1, threads)
-    rate, dt = cpu_port_tokens_per_s(w, rows, steps_run, threads)
-    cfg = {"workload": w.notes, "sample_rows_per_step": rows, "rows_per_step_full": w.batch,
-           "steps_requested": args.steps, "steps_run": steps_run}
-    line = {"impl": "reference", "metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": steps_run, "warmup": args.warmup, "ms_per_step": w.batch / rate * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded randn*3 logits, uniform histories)", "config": cfg,
-            "cpu_baseline": {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": f"{rows} of {w.batch} rows of the headline workload per step, "
-                                       f"{steps_run} steps, numpy restatement of Sampler.select_batch, "
+    B = w.batch
+    _, t1, kind, note = cpu_rate(w, B, 1, threads)                    # warm-up step (also sizes the run)
+    steps_run = int(max(1, min(args.steps, REF_BUDGET_S // max(t1, 1e-6))))
+    rate, dt, kind, note = cpu_rate(w, B, steps_run, threads)
+    cfg = {"workload": w.notes, "global_batch": B, "rows_per_step": B, "same_config": True,
+           "steps_requested": args.steps, "steps_run": steps_run, "threads": threads}
+    if kind == "reference" and any(p.presence_penalty or p.frequency_penalty for p in w.params):
+        cfg["note"] = "the reference has no presence/frequency penalty; its arm applies repetition only"
+    line = {"impl": "reference", "metric": metric_for(args.workload), "value": rate, "unit": UNIT,
+            "n_gpus": args.gpus, "steps": steps_run, "warmup": 1, "ms_per_step": dt / steps_run * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32" if w.logits.element_size() == 4 else "bf16", "data": "synthetic (seeded)", "config": cfg,
+            "cpu_baseline": {"value": rate, "unit": UNIT, "cores": threads, "kind": kind,
+                             "sample": f"all {B} rows per step x {steps_run} steps ({dt:.1f} s), {note}, "
                                        f"{threads} threads"},
             "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -209,58 +286,58 @@ def run_reference(args, world, rank):
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
-def run_e2e(args, world, w, dev, stream):
-    from b200_sampler import B200Sampler
-    B, V, H = w.batch, w.vocab, w.history_len
-    sampler = B200Sampler(device=dev, seed=1)
-    host_logits = w.logits.pin_memory()
-    hists = w.histories
-    u_host = w.uniforms
-    e2e_steps = max(1, min(args.steps, 10))
-    with torch.cuda.stream(stream):
-        for _ in range(2):
-            sampler.select_batch(host_logits, hists, w.params, uniforms=u_host)
+def timed_repeats(world, dev, stream, run_k):
+    """CUDA-event time (ms) of run_k(), which enqueues exactly K steps on
+    `stream`, bracketed by a barrier and a device synchronisation on both
+    sides.  Repeated until >= MIN_TIMED_S has elapsed (the count agreed over
+    ranks); returns the median repeat and all repeats, each the max over
+    ranks."""
+    import math
+
+    def once():
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
         barrier(world)
-        t0 = time.perf_counter()
-        for _ in range(e2e_steps):
-            ids = sampler.select_batch(host_logits, hists, w.params, uniforms=u_host)
-        dt = time.perf_counter() - t0
-    dt = max_over_ranks(world, dt)
-    assert len(ids) == B
-    return {"value": B * world * e2e_steps / dt, "unit": UNIT,
-            "h2d_bytes_per_step": B * V * 4 + B * H * 4 + (B + 1) * 8 + B * 24 + B * 4,
-            "d2h_bytes_per_step": B * 8, "steps": e2e_steps,
-            "path": "B200Sampler.select_batch(pinned host logits, List[List[int]] histories) -> List[int]"}
+        torch.cuda.synchronize(dev)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            run_k()
+            e1.record(stream)
+        stream.synchronize()
+        barrier(world)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1)
+
+    first = once()
+    n = int(max(2, math.ceil(MIN_TIMED_S * 1e3 / max(first, 1e-3))))
+    n = int(max_over_ranks(world, float(n)))
+    ms = [first] + [once() for _ in range(n - 1)]
+    ms = [max_over_ranks(world, m) for m in ms]
+    return statistics.median(ms), ms
 
 
-def run_ours(args, world, rank, local):
+def measure_rows(args, world, dev, w, r0, r1, clk=None):
+    """Device time per step of ns_sample over rows [r0, r1) of workload w:
+    warm-up launches, then CUDA graphs of exactly K launches rotating over
+    N_BUFFERS logits buffers.  Returns (median ms per step, repeats, ids of
+    the first launch on the unrotated logits)."""
     from b200_sampler.sampler import DeviceBatch
-    from b200_sampler.workloads import headline
-
-    dev = torch.device("cuda", local)
-    w = headline(seed=rank)
-    B, V, H = w.batch, w.vocab, w.history_len
-    db = DeviceBatch(w.histories, w.params, dev, uniforms=w.uniforms)
-    bufs = [w.logits.to(dev)]
-    for i in range(1, N_BUFFERS):
-        bufs.append((w.logits.roll(i, dims=1)).to(dev))
-    out = torch.empty(B, dtype=torch.int64, device=dev)
+    rows = slice(r0, r1)
+    db = DeviceBatch(w.histories[r0:r1], w.params[r0:r1], dev, uniforms=w.uniforms[rows])
+    base = w.logits[rows]
+    bufs = [base.to(dev)] + [base.roll(i, dims=1).to(dev) for i in range(1, N_BUFFERS)]
+    out = torch.empty(r1 - r0, dtype=torch.int64, device=dev)
     stream = torch.cuda.Stream(dev)
-
-    # correctness gate on the benchmarked inputs (first rows only)
     with torch.cuda.stream(stream):
         rc = db.launch(bufs[0], out, stream)
     stream.synchronize()
     assert rc == 0, rc
-    assert int(out.min()) >= 0, "a row failed"
-
+    first_ids = out.cpu().tolist()
     with torch.cuda.stream(stream):
         for i in range(max(args.warmup, 3)):
             assert db.launch(bufs[i % N_BUFFERS], out, stream) == 0
     stream.synchronize()
 
-    # CUDA graphs of up to GRAPH_LAUNCHES launches rotating over the buffers;
-    # `reps` replays of the full graph plus one of the remainder make K steps
     def capture(n):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
@@ -271,70 +348,122 @@ def run_ours(args, world, rank, local):
     reps, rem = divmod(args.steps, per)
     g = capture(per)
     g_rem = capture(rem) if rem else None
-    with torch.cuda.stream(stream):
-        g.replay()                                   # graph warm-up
+
+    def run_k():
+        for _ in range(reps):
+            g.replay()
         if g_rem is not None:
             g_rem.replay()
+    with torch.cuda.stream(stream):
+        run_k()                                      # graph warm-up
     stream.synchronize()
-
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize(dev)
-    with ClockSampler(local) as clk:
-        with torch.cuda.stream(stream):
-            e0.record(stream)
-            for _ in range(reps):
-                g.replay()
-            if g_rem is not None:
-                g_rem.replay()
-            e1.record(stream)
-        stream.synchronize()
-    barrier(world)
-    torch.cuda.synchronize(dev)
-    ms = e0.elapsed_time(e1)
-    ms_max = max_over_ranks(world, ms)
-    ms_per_step = ms_max / args.steps
-    tokens_per_s = B * world / (ms_per_step / 1e3)
-
-    peak, peak_kind = _peaks()
-    alg = algorithmic_bytes(B, V, H)
-    achieved = alg / (ms / args.steps / 1e3) / 1e9
+    if clk is not None:
+        with clk:
+            ms, all_ms = timed_repeats(world, dev, stream, run_k)
+    else:
+        ms, all_ms = timed_repeats(world, dev, stream, run_k)
     del g, g_rem
+    return ms / args.steps, [m / args.steps for m in all_ms], first_ids, (per, reps, rem)
 
-    # ---- end to end through the public API, host buffers ----
+
+def run_e2e(args, world, w, dev, r0, r1):
+    from b200_sampler import B200Sampler
+    B, V, H = r1 - r0, w.vocab, w.history_len
+    sampler = B200Sampler(device=dev, seed=1)
+    host_logits = w.logits[r0:r1].contiguous().pin_memory()
+    hists = w.histories[r0:r1]
+    params = w.params[r0:r1]
+    u_host = w.uniforms[r0:r1].contiguous()
+    e2e_steps = max(1, min(args.steps, 10))
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            sampler.select_batch(host_logits, hists, params, uniforms=u_host)
+        barrier(world)
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            ids = sampler.select_batch(host_logits, hists, params, uniforms=u_host)
+        dt = time.perf_counter() - t0
+    dt = max_over_ranks(world, dt)
+    assert len(ids) == B
+    esz = w.logits.element_size()
+    return {"value": w.batch * e2e_steps / dt if world > 1 else B * e2e_steps / dt, "unit": UNIT,
+            "h2d_bytes_per_step": B * V * esz + sum(len(h) for h in hists) * 4 + (B + 1) * 8 + B * 24 + B * 4,
+            "d2h_bytes_per_step": B * 8, "steps": e2e_steps,
+            "path": "B200Sampler.select_batch(pinned host logits, List[List[int]] histories) -> List[int]"}
+
+
+def run_ours(args, world, rank, local):
+    from b200_sampler.workloads import WORKLOADS
+
+    dev = torch.device("cuda", local)
+    w = WORKLOADS[args.workload]()
+    B, V, H = w.batch, w.vocab, w.history_len
+    esz = w.logits.element_size()
+    r0, r1 = rank * B // world, (rank + 1) * B // world
+    clk = ClockSampler(local)
+    ms_step, all_ms, first_ids, (per, reps, rem) = measure_rows(args, world, dev, w, r0, r1, clk)
+    tokens_per_s = B / (ms_step / 1e3)
+    # roofline of the dominant kernel: algorithmic bytes of the rows this
+    # rank launched over the launch's average device time (max over ranks)
+    peak, peak_kind = _peaks()
+    alg = algorithmic_bytes(r1 - r0, V, H, esz)
+    achieved = alg / (ms_step / 1e3) / 1e9
+
+    weak = None
+    if world > 1:
+        ms_w, _, _, _ = measure_rows(args, world, dev, w, 0, B)
+        weak = {"value": B * world / (ms_w / 1e3), "unit": UNIT, "ms_per_step": ms_w,
+                "global_batch": B * world, "rows_per_gpu": B, "scaling": "weak",
+                "note": "every rank samples its own full copy of the batch"}
+
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(args, world, w, dev, stream)
+        e2e = run_e2e(args, world, w, dev, r0, r1)
 
-    line = {"metric": METRIC, "value": tokens_per_s, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded randn*3 logits, uniform histories)",
-            "config": {"workload": w.notes, "global_batch": B * world, "rows_per_gpu": B, "vocab": V,
-                       "parallelism": f"rows sharded, {world} GPU(s), no collective",
-                       "l2": f"{N_BUFFERS} rotating logits buffers ({N_BUFFERS * B * V * 4 / 1e6:.0f} MB) > L2",
-                       "timing": f"CUDA graphs ({per} launches x {reps} replays"
-                                 f"{f' + {rem}' if rem else ''}), CUDA events, max over ranks"},
+    line = {"metric": metric_for(args.workload), "value": tokens_per_s, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32" if esz == 4 else "bf16",
+            "data": "synthetic (seeded)",
+            "config": {"workload": w.notes, "name": args.workload, "global_batch": B, "rows_per_gpu": r1 - r0,
+                       "vocab": V,
+                       "parallelism": f"one batch sharded by rows over {world} GPU(s), no collective",
+                       "l2": f"{N_BUFFERS} rotating logits buffers ({N_BUFFERS * (r1 - r0) * V * esz / 1e6:.0f} MB "
+                             f"per GPU; > the 126 MB L2 when above it)",
+                       "timing": f"CUDA graphs ({per} launches x {reps} replays{f' + {rem}' if rem else ''}) "
+                                 f"= K steps per repeat, {len(all_ms)} repeats >= {MIN_TIMED_S:.0f} s, median "
+                                 f"repeat, CUDA events, max over ranks",
+                       "ms_per_step_repeats": [round(m, 6) for m in all_ms]},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": NCU_TRAFFIC_BYTES, "peak_kind": peak_kind,
-                         "algorithmic_bytes_per_launch": alg,
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
-                                           "(profiles/sample_kernel_headline_B256.md)"},
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": NCU_TRAFFIC_BYTES if (args.workload == "headline" and world == 1) else None,
+                         "traffic_source": NCU_TRAFFIC_SOURCE if (args.workload == "headline" and world == 1)
+                         else "not recorded for this workload",
+                         "algorithmic_bytes_per_launch": alg},
             "gpu_launches": args.steps}
+    if weak is not None:
+        line["weak_scaling"] = weak
     if e2e is not None:
         line["e2e"] = e2e
     clocks = clk.summary()
     if clocks is not None:
         line["clocks"] = clocks
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        # bounded sample: rows of the same workload until ~10 s of single-thread work
-        probe, _ = cpu_port_tokens_per_s(w, 2, 1, 1)
-        rows = int(max(2, min(w.batch, probe * 10.0)))
-        reps_c = int(max(1, min(100, 10.0 * probe / rows)))
-        rate, dtc = cpu_port_tokens_per_s(w, rows, reps_c, 1)
-        line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": 1, "kind": "port",
-                                "sample": f"{rows} of {w.batch} rows of the headline workload x {reps_c} "
-                                          f"({dtc:.1f} s), numpy restatement of Sampler.select_batch, 1 thread"}
+        # parity of every row of the benchmarked launch, then the CPU sampler
+        # on a bounded sample (~10-30 s) at all host threads
+        gate = parity_gate(w, first_ids)
+        line["parity"] = gate
+        threads = os.cpu_count() or 1
+        rows = min(B, 16)
+        _, t1, _, _ = cpu_rate(w, rows, 1, threads)
+        rows = int(min(B, max(rows, rows * 10.0 / max(t1, 1e-6))))
+        rate, dtc, kind, note = cpu_rate(w, rows, 1, threads)
+        line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": threads, "kind": kind,
+                                "sample": f"{rows} of {B} rows of the workload, one select_batch "
+                                          f"({dtc:.1f} s), {note}, {threads} threads"}
+        if not gate["ok"]:
+            print(json.dumps(line), flush=True)
+            raise SystemExit(f"parity gate failed: {gate}")
     if rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -425,24 +554,17 @@ def run_vp(args, world, rank, local):
     with torch.cuda.stream(side):
         g.replay()
     torch.cuda.synchronize(dev)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize(dev)
+
+    def run_k():
+        for _ in range(reps):
+            g.replay()
+        if g_rem is not None:
+            g_rem.replay()
     with ClockSampler(local) as clk:
-        with torch.cuda.stream(side):
-            e0.record(side)
-            for _ in range(reps):
-                g.replay()
-            if g_rem is not None:
-                g_rem.replay()
-            e1.record(side)
-        torch.cuda.synchronize(dev)
-    barrier(world)
+        ms, all_ms = timed_repeats(world, dev, side, run_k)
     del g, g_rem  # graphs holding NCCL calls go before the process group
     if peer:
         ex.release(side)
-    ms = max_over_ranks(world, e0.elapsed_time(e1))
     ms_per_step = ms / args.steps
     peak, peak_kind = _peaks()
     local_bytes = B * width * 4
@@ -455,7 +577,8 @@ def run_vp(args, world, rank, local):
                        "transport": ("peer: records read in place over NVLink by the merge kernel after a "
                                      "flag signal" if peer else "gather: NCCL all-gather of the records"),
                        "timing": f"CUDA graphs of local + exchange + merge ({per} steps x {reps}"
-                                 f"{f' + {rem}' if rem else ''}), CUDA events, max over ranks"},
+                                 f"{f' + {rem}' if rem else ''}) = K steps per repeat, {len(all_ms)} repeats "
+                                 f">= {MIN_TIMED_S:.0f} s, median repeat, CUDA events, max over ranks"},
             "roofline": {"bound": "hbm", "achieved": local_bytes / (ms_per_step / 1e3) / 1e9, "peak": peak,
                          "unit": "GB/s", "frac": local_bytes / (ms_per_step / 1e3) / 1e9 / peak,
                          "traffic": None, "peak_kind": peak_kind, "algorithmic_bytes_per_launch": local_bytes},
@@ -467,18 +590,104 @@ def run_vp(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_decode(args, world, rank, local):
+    """an end-to-end decode loop.  A Qwen3-0.6B-shaped
+    model (28 layers, hidden 1024, 16 query / 8 KV heads, head_dim 128,
+    vocab 151936; transformers' Qwen3 with random-init bf16 weights), batch
+    64, 128-token random prompts, 256 decode steps, each sampled through
+    ``B200Sampler.select_batch_tensor`` with top-k 20 / top-p 0.8 / T 0.7 and
+    the growing histories.  The sampler reads ``logits[:, -1, :]`` of the
+    model's bf16 [B, S, V] output in place (row stride S x V) -- the
+    reference stacks ``.float()`` copies of those rows
+    (inferencer/torch_inferencer.py:242-251).  Reports decode tokens/s and
+    the sampler's share of the step time (CUDA events around each call).
+    One GPU; with N ranks each runs its own replica."""
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    from b200_sampler import B200Sampler
+    from b200_sampler.params import SamplingParams
+
+    dev = torch.device("cuda", local)
+    B, P, steps = 64, 128, args.decode_steps
+    cfg = Qwen3Config(vocab_size=151936, hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
+                      num_attention_heads=16, num_key_value_heads=8, head_dim=128,
+                      max_position_embeddings=P + steps + 8, tie_word_embeddings=True)
+    torch.manual_seed(1234 + rank)
+    with torch.device(dev):
+        model = Qwen3ForCausalLM(cfg).to(torch.bfloat16).eval()
+    g = torch.Generator().manual_seed(99 + rank)
+    prompt = torch.randint(0, cfg.vocab_size, (B, P), generator=g)
+    params = [SamplingParams(temperature=0.7, top_k=20, top_p=0.8)] * B
+    sampler = B200Sampler(device=dev, seed=5 + rank)
+    e_s = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    e_e = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+
+    def generate(n_steps, timed):
+        hist = [list(map(int, r)) for r in prompt]
+        ids = prompt.to(dev)
+        with torch.inference_mode():
+            out = model(input_ids=ids, use_cache=True)
+            pkv = out.past_key_values
+            x = out.logits[:, -1, :]                     # [B, V] bf16 view, row stride P x V
+            assert x.stride(1) == 1 and x.stride(0) == P * cfg.vocab_size
+            for t in range(n_steps + 1):
+                if timed:
+                    e_s[t].record()
+                nxt = sampler.select_batch_tensor(x, hist, params)
+                if timed:
+                    e_e[t].record()
+                new = nxt.tolist()
+                assert min(new) >= 0, new
+                for b in range(B):
+                    hist[b].append(new[b])
+                if t == n_steps:
+                    break
+                out = model(input_ids=nxt[:, None], past_key_values=pkv, use_cache=True)
+                pkv = out.past_key_values
+                x = out.logits[:, -1, :]
+        return hist
+
+    generate(4, False)                                   # warm-up
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    t0 = time.perf_counter()
+    hist = generate(steps, True)
+    torch.cuda.synchronize(dev)
+    dt = time.perf_counter() - t0
+    sampler_ms = sum(a.elapsed_time(b) for a, b in zip(e_s, e_e))
+    dt = max_over_ranks(world, dt)
+    line = {"metric": "end-to-end decode tokens/sec, Qwen3-0.6B shape (BASELINE config 5)",
+            "value": B * world * (steps + 1) / dt, "unit": UNIT, "n_gpus": world, "steps": steps,
+            "warmup": 4, "ms_per_step": dt / (steps + 1) * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, random prompts)",
+            "config": {"workload": f"Qwen3-0.6B shape, B={B}, {P}-token prompts, {steps} decode steps, "
+                                   "k=20 p=0.8 T=0.7, histories = prompt + outputs",
+                       "model": "transformers Qwen3ForCausalLM (eager, DynamicCache), random init bf16",
+                       "sampler_feed": "logits[:, -1, :] of the bf16 [B, S, V] output, in place via row_stride"},
+            "sampler": {"ms_total": sampler_ms, "share_of_step_time": sampler_ms / 1e3 / dt,
+                        "ms_per_call": sampler_ms / (steps + 1),
+                        "note": "CUDA events around select_batch_tensor (host packing of the growing "
+                                "histories, H2D, the kernel)"},
+            "tokens_generated_per_row": len(hist[0]) - P}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
+    from b200_sampler.workloads import WORKLOADS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--steps", type=int, default=5000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="headline", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
     ap.add_argument("--vp-transport", default="peer", choices=["peer", "gather"],
                     help="vp mode: records read in place over NVLink (peer) or all-gathered (gather)")
-    ap.add_argument("--mode", default="rows", choices=["rows", "vp"],
-                    help="rows: the headline (rows sharded); vp: vocab-parallel config 4")
+    ap.add_argument("--mode", default="rows", choices=["rows", "vp", "decode"],
+                    help="rows: the workload sharded by rows; vp: vocab-parallel config 4; "
+                         "decode: the config 5 decode loop")
+    ap.add_argument("--decode-steps", type=int, default=256)
     args = ap.parse_args()
     world, rank, local = (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
                           int(os.environ.get("LOCAL_RANK", "0")))
@@ -489,6 +698,8 @@ def main():
     try:
         if args.mode == "vp":
             run_vp(args, world, rank, local)
+        elif args.mode == "decode":
+            run_decode(args, world, rank, local)
         else:
             run_ours(args, world, rank, local)
     finally:

@@ -117,6 +117,23 @@ int ns_sample(const void* logits, int dtype, int64_t batch, int64_t vocab, int64
               int64_t* out_ids, void* workspace, size_t workspace_bytes, ns_stream_t stream);
 
 /*
+ * Debug readback: the penalised logits of whole rows, fp32, for bit-exact
+ * comparison with a reference.  out[b * out_stride + j] = logits[b][j] widened
+ * to fp32, then for every distinct id of row b's history the value the
+ * sampling kernels use: repetition (x * rep if x < 0 else x / rep), then
+ * x - frequency * count, then x - presence, each rounded to fp32.  No
+ * temperature.  row_status int32 [batch]: NS_OK or
+ * NS_ERR_TOKEN_ID_OUT_OF_RANGE (that row of out holds only the widened
+ * logits).  O(history^2) per row: a checking tool, not a hot path.
+ * Replaces: Sampler._apply_repetition_penalty (sampler.py:93-108) as a
+ *   standalone step (the reference applies it in place at sampler.py:52-57).
+ */
+int ns_penalize_debug(const void* logits, int dtype, int64_t batch, int64_t vocab, int64_t row_stride,
+                      const int32_t* hist_ids, const int64_t* hist_offsets, const float* repetition_penalty,
+                      const float* presence_penalty, const float* frequency_penalty, float* out,
+                      int64_t out_stride, int32_t* row_status, ns_stream_t stream);
+
+/*
  * Vocab-parallel sampling (tensor-parallel lm_head output: each device holds
  * a contiguous column slice of every row).  No reference counterpart: the
  * reference samples whole rows only (sampler.py:36-91); these calls split that

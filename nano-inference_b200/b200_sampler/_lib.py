@@ -71,6 +71,12 @@ PROTOTYPES = {
         _c_vp, _c_u64, _c_u64,                       # uniforms, philox_seed, philox_offset
         _c_vp, _c_vp,                                # out_ids, stream
     ]),
+    "ns_penalize_debug": (_c_int, [
+        _c_vp, _c_int, _c_i64, _c_i64, _c_i64,       # logits, dtype, batch, vocab, row_stride
+        _c_vp, _c_vp,                                # hist_ids, hist_offsets
+        _c_vp, _c_vp, _c_vp,                         # repetition, presence, frequency penalties
+        _c_vp, _c_i64, _c_vp, _c_vp,                 # out, out_stride, row_status, stream
+    ]),
     "ns_vp_peer_alloc": (_c_int, [_c_sz, ctypes.POINTER(_c_vp)]),
     "ns_vp_peer_free": (_c_int, [_c_vp]),
     "ns_ipc_handle": (_c_int, [_c_vp, _c_vp]),

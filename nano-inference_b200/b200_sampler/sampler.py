@@ -205,6 +205,38 @@ class B200Sampler(SamplerBase):
             raise RuntimeError(f"ns_sample failed: {_lib.status_string(rc)}")
         return out
 
+    def penalized_logits(self, logits: torch.Tensor, all_generated_ids: Optional[Sequence[Sequence[int]]],
+                         all_sampling_params) -> torch.Tensor:
+        """Debug readback: fp32 [B, V] logits after the history penalties
+        (repetition, frequency, presence; no temperature), bit for bit the
+        values the sampling kernels use (``ns_penalize_debug``).  The
+        reference applies the repetition step in place (sampler.py:52-57,
+        93-108).  A history id outside [0, V) raises IndexError."""
+        if logits.dim() != 2 or logits.dtype not in _DTYPES:
+            raise ValueError("expected [batch, vocab] fp32 / bf16 / fp16 logits")
+        B, V = int(logits.shape[0]), int(logits.shape[1])
+        device = self._device_for(logits)
+        stream = torch.cuda.current_stream(device)
+        if logits.device != device or logits.stride(1) != 1:
+            logits = logits.to(device).contiguous()
+        out = torch.empty(B, V, dtype=torch.float32, device=device)
+        status = torch.empty(B, dtype=torch.int32, device=device)
+        if B == 0:
+            return out
+        with self._lock:
+            st = self._stage(device, B, all_generated_ids, all_sampling_params, None, stream)
+            rc = self.lib.ns_penalize_debug(
+                logits.data_ptr(), _DTYPES[logits.dtype], B, V, int(logits.stride(0)),
+                st.hist_ids, st.hist_offsets, st.p32 + 12 * B, st.p32 + 16 * B, st.p32 + 20 * B,
+                out.data_ptr(), V, status.data_ptr(), stream.cuda_stream)
+            st.keep_alive(stream)
+        if rc != _lib.NS_OK:
+            raise RuntimeError(f"ns_penalize_debug failed: {_lib.status_string(rc)}")
+        bad = [int(v) for v in status.tolist() if v != _lib.NS_OK]
+        if bad:
+            raise _ROW_ERRORS.get(bad[0], RuntimeError)(_lib.status_string(bad[0]))
+        return out
+
     def _stage(self, device: torch.device, B: int, all_generated_ids, all_sampling_params,
                uniforms: Optional[torch.Tensor], stream: torch.cuda.Stream) -> "_Staged":
         """Pack params [6, B], the history CSR (only when a row has a

@@ -27,7 +27,8 @@ rank).
 from __future__ import annotations
 
 import ctypes
-from typing import List, Optional, Sequence
+import time
+from typing import Callable, List, Optional, Sequence, Tuple
 
 import numpy as np
 import torch
@@ -40,6 +41,30 @@ from .workspace import Workspace
 
 FAST_MAX_K = 240       # largest top_k the candidate records serve (kFastK in the kernel)
 MAX_CAP = 1024         # record capacity limit (kRankMax in the kernel)
+PEER_WAIT_S = 30.0     # host-side wait for late peers after the merge kernel's own ~200 ms bound
+
+
+def wait_for_peers(read_state: Callable[[], Tuple[Sequence[int], int]], timeout_s: float,
+                   poll_s: float = 0.002) -> bool:
+    """Poll ``read_state() -> (flags, epoch)`` until every rank's flag has
+    reached this rank's step count; False if that does not happen within
+    ``timeout_s`` seconds."""
+    deadline = time.monotonic() + timeout_s
+    while True:
+        flags, epoch = read_state()
+        if all(int(f) >= int(epoch) for f in flags):
+            return True
+        if time.monotonic() >= deadline:
+            return False
+        time.sleep(poll_s)
+
+
+class _DeviceWords:
+    """int64 words of raw device memory, viewed as a tensor (no ownership)."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<i8", "data": (ptr, False),
+                                         "version": 3, "strides": None}
 
 
 def gather_records(rec: torch.Tensor, group=None) -> torch.Tensor:
@@ -140,6 +165,14 @@ class PeerExchange:
         """This rank's step counter (device memory, advanced by ns_vp_signal)."""
         return self.flags(self.rank) + 8 * self.world
 
+    def read_state(self, stream: torch.cuda.Stream) -> Tuple[List[int], int]:
+        """(every rank's flag in this rank's buffer, this rank's step count),
+        read on the host once `stream`'s work is done."""
+        stream.synchronize()
+        words = torch.as_tensor(_DeviceWords(self.flags(self.rank), self.world + 1), device=self.device)
+        v = words.cpu().tolist()
+        return v[:self.world], v[self.world]
+
 
 def _ptr_array(ptrs: Sequence[int]) -> ctypes.c_void_p:
     arr = (ctypes.c_void_p * len(ptrs))(*ptrs)
@@ -196,6 +229,25 @@ class VocabParallelSampler(B200Sampler):
             raise ValueError(f"unknown transport {transport!r}")
         self.transport = transport
         self._exchange: Optional[PeerExchange] = None
+        self._broken: Optional[str] = None   # set when a peer never signalled: every later call raises
+        self.peer_wait_s = PEER_WAIT_S
+
+    def _recover_timeout(self, ex: PeerExchange, stream: torch.cuda.Stream, merge, out: torch.Tensor) -> int:
+        """The merge kernel gave up waiting (~200 ms) for a peer's flag.  Host
+        skew (a slow first call, a garbage collection) is not a failure: wait
+        on the host, up to ``peer_wait_s``, for every flag to reach this step,
+        then merge again.  A peer that never signals makes the exchange
+        unusable: this call and every later one raise."""
+        if not wait_for_peers(lambda: ex.read_state(stream), self.peer_wait_s):
+            flags, epoch = ex.read_state(stream)
+            late = [r for r, f in enumerate(flags) if f < epoch]
+            self._broken = f"rank(s) {late} did not signal step {epoch} within {self.peer_wait_s:.1f} s"
+            raise RuntimeError(f"vocab-parallel exchange timed out: {self._broken}")
+        rc = merge()
+        if rc == _lib.NS_OK and bool((out == _lib.NS_ERR_DEVICE_TIMEOUT).any()):
+            self._broken = "the merge timed out again after every flag was set"
+            raise RuntimeError(f"vocab-parallel exchange timed out: {self._broken}")
+        return rc
 
     def close(self):
         """Collective: release the peer-exchange buffers (every rank calls it)."""
@@ -210,6 +262,8 @@ class VocabParallelSampler(B200Sampler):
 
     def _run(self, logits, all_generated_ids, all_sampling_params, uniforms, out, retry: bool,
              cap: Optional[int] = None, offset: Optional[int] = None) -> torch.Tensor:
+        if self._broken is not None:
+            raise RuntimeError(f"vocab-parallel exchange is unusable: {self._broken}")
         if logits.dim() != 2 or logits.shape[1] != self.vocab_local:
             raise ValueError("expected this rank's [batch, vocab_local] slice")
         if logits.dtype not in _DTYPES:
@@ -272,10 +326,15 @@ class VocabParallelSampler(B200Sampler):
                 if rc != _lib.NS_OK:
                     raise RuntimeError(f"ns_vp_signal failed: {_lib.status_string(rc)}")
                 recs, _keep2 = _ptr_array([ex.record(r, par) for r in range(self.world)])
-                rc = self.lib.ns_vp_merge_peers(
-                    recs, self.world, ex.flags(self.rank), ex.counter(), B, cap, self.vocab_total,
-                    st.p32, st.p32 + 4 * B, st.p32 + 8 * B, st.u_ptr, self.seed, offset,
-                    out.data_ptr(), stream.cuda_stream)
+
+                def merge():
+                    return self.lib.ns_vp_merge_peers(
+                        recs, self.world, ex.flags(self.rank), ex.counter(), B, cap, self.vocab_total,
+                        st.p32, st.p32 + 4 * B, st.p32 + 8 * B, st.u_ptr, self.seed, offset,
+                        out.data_ptr(), stream.cuda_stream)
+                rc = merge()
+                if rc == _lib.NS_OK and bool((out == _lib.NS_ERR_DEVICE_TIMEOUT).any()):
+                    rc = self._recover_timeout(ex, stream, merge, out)
             else:
                 gathered = gather_records(rec, self.group)
                 rc = self.lib.ns_vp_merge(

@@ -125,3 +125,51 @@ def config4(seed: int = 0, batch: int = 128) -> Workload:
     p = SamplingParams(temperature=0.8, top_k=50, top_p=0.95)
     return Workload("c4", batch, V, make_logits(seed, batch, V, 3.0),
                     [[] for _ in range(batch)], [p] * batch, make_uniforms(1, batch))
+
+
+def topp095(seed: int = 0, batch: int = 256) -> Workload:
+    """Top-p only (top-k off), p 0.95, T 1.0, no penalties: the common
+    production setting, fp32 ``randn*3``."""
+    V = QWEN_VOCAB
+    p = SamplingParams(temperature=1.0, top_p=0.95)
+    return Workload("topp095", batch, V, make_logits(seed, batch, V, 3.0), [[] for _ in range(batch)],
+                    [p] * batch, make_uniforms(1, batch),
+                    notes="B=%d V=%d fp32 randn*3 T=1.0 top-k off p=0.95, no penalties" % (batch, V))
+
+
+def softmax_only(seed: int = 0, batch: int = 256) -> Workload:
+    """Plain multinomial draw: T 1.0, top-k and top-p off, no penalties."""
+    V = QWEN_VOCAB
+    p = SamplingParams(temperature=1.0)
+    return Workload("softmax", batch, V, make_logits(seed, batch, V, 3.0), [[] for _ in range(batch)],
+                    [p] * batch, make_uniforms(1, batch),
+                    notes="B=%d V=%d fp32 randn*3 T=1.0, top-k / top-p off, no penalties" % (batch, V))
+
+
+def k240(seed: int = 0, batch: int = 256) -> Workload:
+    """The headline with top-k 240 (the largest single-pass top-k)."""
+    w = headline(batch=batch, seed=seed)
+    p = SamplingParams(temperature=0.7, top_k=240, top_p=0.9, repetition_penalty=1.1,
+                       presence_penalty=0.5, frequency_penalty=0.3)
+    w.name, w.params = "k240", [p] * batch
+    w.notes = w.notes.replace("k=50", "k=240")
+    return w
+
+
+def _with_notes(w: Workload, notes: str) -> Workload:
+    w.notes = notes
+    return w
+
+
+# Named workloads of the benchmark (``bench.py --workload``).
+WORKLOADS = {
+    "headline": lambda: headline(),
+    "c1": lambda: _with_notes(config1(), "C1: B=8 V=151936 fp32 randn*3 T=0.7 k=50 p=0.9 rep=1.1 H=64"),
+    "c2": lambda: _with_notes(config2(), "C2: B=64 V=151936 bf16 randn*2 greedy, rep=1.2 pres=0.5 freq=0.3, "
+                                         "H=512 Zipf(1.1)"),
+    "c3": lambda: _with_notes(config3(), "C3: B=256 V=151936 fp32 randn*3 + 5% spikes, per-row T U[0.3,1.5] "
+                                         "k U{1..200} p U[0.5,1], rep=1.1 pres=0.5 freq=0.3, H=1024"),
+    "topp095": lambda: topp095(),
+    "softmax": lambda: softmax_only(),
+    "k240": lambda: k240(),
+}

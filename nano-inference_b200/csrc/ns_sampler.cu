@@ -4465,6 +4465,72 @@ static int vp_merge_launch(const KArgs& a, const VpMerge& v, ns_stream_t stream)
   return NS_OK;
 }
 
+
+// ---------------------------------------------------------------------------
+// debug readback: the penalised logits of whole rows
+// ---------------------------------------------------------------------------
+// One block per row.  The row is widened to fp32 into out; then every history
+// position counts the occurrences of its id in the row's history (chunks of
+// the ids staged in shared memory) and the first occurrence of each distinct
+// id writes penalize(x, count) -- the same device function, hence the same
+// bits, as the sampling kernels.  O(H^2 / threads) per row: a checking tool,
+// not a hot path.
+constexpr int kPenChunk = 4096;
+
+template <int DT>
+__global__ void __launch_bounds__(kThreads) penalize_rows_kernel(const __grid_constant__ KArgs a, float* out,
+                                                                 int64_t out_stride, int32_t* row_status) {
+  using E = Elem<DT>;
+  __shared__ int ids_s[kPenChunk];
+  __shared__ int bad;
+  const int64_t row = blockIdx.x;
+  const typename E::raw* src = reinterpret_cast<const typename E::raw*>(a.logits) + row * a.row_stride;
+  float* dst = out + row * out_stride;
+  for (int64_t j = threadIdx.x; j < a.vocab; j += kThreads) dst[j] = E::widen(src[j]);
+  if (threadIdx.x == 0) bad = 0;
+  __syncthreads();
+  const float rep = a.rep ? a.rep[row] : 1.0f;
+  const float pres = a.pres ? a.pres[row] : 0.0f;
+  const float freq = a.freq ? a.freq[row] : 0.0f;
+  const int64_t h0 = a.hist_offsets ? a.hist_offsets[row] : 0, h1 = a.hist_offsets ? a.hist_offsets[row + 1] : 0;
+  const bool active = (rep != 1.0f || pres != 0.0f || freq != 0.0f) && h1 > h0;
+  if (active) {
+    for (int64_t i = h0 + threadIdx.x; i < h1; i += kThreads) {
+      const int id = a.hist_ids[i];
+      if (id < 0 || int64_t(id) >= a.vocab) atomicOr(&bad, 1);
+    }
+  }
+  __syncthreads();
+  if (bad) {
+    if (threadIdx.x == 0) row_status[row] = NS_ERR_TOKEN_ID_OUT_OF_RANGE;
+    return;
+  }
+  if (active) {
+    const int64_t n = h1 - h0;
+    for (int64_t mine0 = 0; mine0 < n; mine0 += kThreads) {  // every thread takes part in the staging
+      const int64_t mi = mine0 + threadIdx.x;
+      const int my = (mi < n) ? a.hist_ids[h0 + mi] : -1;
+      int cnt = 0;
+      bool first = true;
+      for (int64_t c0 = 0; c0 < n; c0 += kPenChunk) {
+        const int cn = int((n - c0 < int64_t(kPenChunk)) ? (n - c0) : int64_t(kPenChunk));
+        __syncthreads();
+        for (int k = threadIdx.x; k < cn; k += kThreads) ids_s[k] = a.hist_ids[h0 + c0 + k];
+        __syncthreads();
+        if (mi < n) {
+          for (int k = 0; k < cn; ++k) {
+            const bool eq = ids_s[k] == my;
+            cnt += eq ? 1 : 0;
+            if (eq && c0 + k < mi) first = false;
+          }
+        }
+      }
+      if (mi < n && first) dst[my] = penalize(E::widen(src[my]), cnt, rep, pres, freq);
+    }
+  }
+  if (threadIdx.x == 0) row_status[row] = NS_OK;
+}
+
 }  // namespace ns
 
 // ---------------------------------------------------------------------------
@@ -4547,6 +4613,39 @@ int ns_sample(const void* logits, int dtype, int64_t batch, int64_t vocab, int64
     case NS_DTYPE_BF16: return ns::launch<NS_DTYPE_BF16>(a, batch, stream);
     default: return ns::launch<NS_DTYPE_F16>(a, batch, stream);
   }
+}
+
+int ns_penalize_debug(const void* logits, int dtype, int64_t batch, int64_t vocab, int64_t row_stride,
+                      const int32_t* hist_ids, const int64_t* hist_offsets, const float* repetition_penalty,
+                      const float* presence_penalty, const float* frequency_penalty, float* out,
+                      int64_t out_stride, int32_t* row_status, ns_stream_t stream) {
+  if (dtype != NS_DTYPE_F32 && dtype != NS_DTYPE_BF16 && dtype != NS_DTYPE_F16) return NS_ERR_UNSUPPORTED_DTYPE;
+  if (batch < 0 || vocab <= 0 || row_stride < vocab || out_stride < vocab) return NS_ERR_INVALID_ARGUMENT;
+  if (vocab > (int64_t(1) << 24) || batch > (int64_t(1) << 24)) return NS_ERR_INVALID_ARGUMENT;
+  if ((hist_ids == nullptr) != (hist_offsets == nullptr)) return NS_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return NS_OK;
+  if (!logits || !out || !row_status) return NS_ERR_INVALID_ARGUMENT;
+  ns::KArgs a = {};
+  a.logits = logits;
+  a.vocab = vocab;
+  a.row_stride = row_stride;
+  a.hist_ids = hist_ids;
+  a.hist_offsets = hist_offsets;
+  a.rep = repetition_penalty;
+  a.pres = presence_penalty;
+  a.freq = frequency_penalty;
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case NS_DTYPE_F32:
+      ns::penalize_rows_kernel<NS_DTYPE_F32><<<unsigned(batch), ns::kThreads, 0, s>>>(a, out, out_stride, row_status);
+      break;
+    case NS_DTYPE_BF16:
+      ns::penalize_rows_kernel<NS_DTYPE_BF16><<<unsigned(batch), ns::kThreads, 0, s>>>(a, out, out_stride, row_status);
+      break;
+    default:
+      ns::penalize_rows_kernel<NS_DTYPE_F16><<<unsigned(batch), ns::kThreads, 0, s>>>(a, out, out_stride, row_status);
+  }
+  return cudaGetLastError() == cudaSuccess ? NS_OK : NS_ERR_CUDA;
 }
 
 int ns_vp_record_int64s(int64_t batch, int cap, int64_t* out_count) {

@@ -106,3 +106,20 @@ def test_top_k_225_to_240_one_block_per_row(sampler, dtype):
     ids = sampler.select_batch_tensor(x.cuda(), hs, params, uniforms=u.cuda()).cpu().tolist()
     ref = O.sample_batch(x.float().numpy(), hs, params, uniforms=u.numpy())
     assert _check(ids, ref, f"k 225..240 {dtype}") <= 4
+
+
+def test_last_position_of_a_bsv_tensor_in_place(sampler):
+    """The decode step's feed: ``logits[:, -1, :]`` of a bf16 [B, S, V] model
+    output, read in place through the row stride S x V (the reference stacks
+    ``.float()`` copies of these rows, inferencer/torch_inferencer.py:242-251)."""
+    B, S, V = 16, 5, 151936
+    full = make_logits(400, B * S, V, 2.0).view(B, S, V).to(torch.bfloat16).cuda()
+    x = full[:, -1, :]
+    assert x.stride() == (S * V, 1)
+    hs = make_histories(401, B, V, 300)
+    params = [SamplingParams(temperature=0.7, top_k=20, top_p=0.8, repetition_penalty=1.1) if b % 3
+              else SamplingParams(temperature=0.0, repetition_penalty=1.2) for b in range(B)]
+    u = make_uniforms(402, B)
+    ids = sampler.select_batch_tensor(x, hs, params, uniforms=u.cuda()).cpu().tolist()
+    ref = O.sample_batch(x.float().cpu().numpy(), hs, params, uniforms=u.numpy())
+    assert _check(ids, ref, "[B,S,V] last position") <= 1
