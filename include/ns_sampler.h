@@ -117,6 +117,43 @@ int ns_sample(const void* logits, int dtype, int64_t batch, int64_t vocab, int64
               int64_t* out_ids, void* workspace, size_t workspace_bytes, ns_stream_t stream);
 
 /*
+ * ns_sample for callers that cannot allocate device memory.  No counterpart
+ * in the reference: it is an addition of this library.
+ *
+ * Some callers may not call cudaMalloc (or any allocating routine) around a
+ * sampling step: an engine whose device memory is carved up once at start-up
+ * by its own pool, a plug-in living inside a host runtime that owns all
+ * allocation, or code that must not allocate between steps.  This call takes
+ * the same arguments as ns_sample except the workspace, and uses a scratch
+ * array of NS_NOALLOC_SCRATCH_BYTES that is part of the library itself (a
+ * fixed device array that every GPU which loads the library holds until the
+ * process exits).
+ *
+ *   - A call whose ns_sampler_workspace_bytes(batch, vocab, max_history) is
+ *     larger than NS_NOALLOC_SCRATCH_BYTES is refused with
+ *     NS_ERR_WORKSPACE_TOO_SMALL before anything is launched.  Up to
+ *     max_history 1024 no scratch is needed at all; at vocab 151936 and one
+ *     block per row the limit allows about batch x max_history <= 1.39 M
+ *     (for example batch 256 with histories of up to 5461 ids).
+ *   - The first call on a device looks up that device's address of the
+ *     array (no allocation); make that first call before any stream capture.
+ *   - Every call on a device uses the same array.  The kernel clears what
+ *     it needs before it reads it, so no call depends on what an earlier one
+ *     left there, but two calls that overlap on the GPU (different streams
+ *     without ordering) race on it: serialise them.
+ *   - It calls no cudaMalloc, cudaFree or other allocating routine.
+ */
+#define NS_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+
+int ns_sample_noalloc(const void* logits, int dtype, int64_t batch, int64_t vocab, int64_t row_stride,
+                      const int32_t* hist_ids, const int64_t* hist_offsets, int64_t max_history,
+                      const float* temperature, const int32_t* top_k, const float* top_p,
+                      const float* repetition_penalty, const float* presence_penalty,
+                      const float* frequency_penalty,
+                      const float* uniforms, uint64_t philox_seed, uint64_t philox_offset,
+                      int64_t* out_ids, ns_stream_t stream);
+
+/*
  * Debug readback: the penalised logits of whole rows, fp32, for bit-exact
  * comparison with a reference.  out[b * out_stride + j] = logits[b][j] widened
  * to fp32, then for every distinct id of row b's history the value the

@@ -14,6 +14,7 @@ from .build import LIB_PATH
 
 NS_OK = 0
 NS_IPC_HANDLE_BYTES = 64
+NS_NOALLOC_SCRATCH_BYTES = 16 << 20     # include/ns_sampler.h
 NS_ERR_INVALID_ARGUMENT = -1
 NS_ERR_WORKSPACE_TOO_SMALL = -2
 NS_ERR_UNSUPPORTED_DTYPE = -3
@@ -47,6 +48,14 @@ PROTOTYPES = {
         _c_vp, _c_vp, _c_vp,                         # repetition, presence, frequency
         _c_vp, _c_u64, _c_u64,                       # uniforms, philox_seed, philox_offset
         _c_vp, _c_vp, _c_sz, _c_vp,                  # out_ids, workspace, workspace_bytes, stream
+    ]),
+    "ns_sample_noalloc": (_c_int, [
+        _c_vp, _c_int, _c_i64, _c_i64, _c_i64,       # logits, dtype, batch, vocab, row_stride
+        _c_vp, _c_vp, _c_i64,                        # hist_ids, hist_offsets, max_history
+        _c_vp, _c_vp, _c_vp,                         # temperature, top_k, top_p
+        _c_vp, _c_vp, _c_vp,                         # repetition, presence, frequency
+        _c_vp, _c_u64, _c_u64,                       # uniforms, philox_seed, philox_offset
+        _c_vp, _c_vp,                                # out_ids, stream
     ]),
     "ns_vp_record_int64s": (_c_int, [_c_i64, _c_int, ctypes.POINTER(_c_i64)]),
     "ns_vp_local": (_c_int, [

@@ -4817,3 +4817,63 @@ int ns_ipc_close(void* ptr) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// ns_sample without a caller workspace
+// ---------------------------------------------------------------------------
+// For callers that may not allocate device memory around a sampling step (an
+// engine whose memory pool owns every byte, a plug-in inside a runtime that
+// does all allocation).  The scratch ns_sample takes from its caller -- the
+// long-history rank arrays -- lives instead in this fixed array, which the
+// CUDA module holds on every device that loads it until the process exits.
+// In host code `g_noalloc_scratch` names a host-side stand-in, not device
+// memory: the device address comes from cudaGetSymbolAddress, looked up once
+// per device with that device current, on its first call.
+namespace ns {
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NS_NOALLOC_SCRATCH_BYTES];
+
+static void* g_noalloc_addr[64];
+
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return NS_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
+      (void)cudaGetLastError();
+      return NS_ERR_CUDA;
+    }
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return NS_OK;
+}
+
+}  // namespace ns
+
+extern "C" {
+
+int ns_sample_noalloc(const void* logits, int dtype, int64_t batch, int64_t vocab, int64_t row_stride,
+                      const int32_t* hist_ids, const int64_t* hist_offsets, int64_t max_history,
+                      const float* temperature, const int32_t* top_k, const float* top_p,
+                      const float* repetition_penalty, const float* presence_penalty,
+                      const float* frequency_penalty, const float* uniforms, uint64_t philox_seed,
+                      uint64_t philox_offset, int64_t* out_ids, ns_stream_t stream) {
+  if (dtype != NS_DTYPE_F32 && dtype != NS_DTYPE_BF16 && dtype != NS_DTYPE_F16) return NS_ERR_UNSUPPORTED_DTYPE;
+  if (batch < 0 || vocab <= 0 || row_stride < vocab || max_history < 0) return NS_ERR_INVALID_ARGUMENT;
+  // the same sizing ns_sample checks a caller workspace against
+  size_t need = 0;
+  if (const int rc = ns_sampler_workspace_bytes(batch, vocab, hist_ids ? max_history : 0, &need)) return rc;
+  if (need > NS_NOALLOC_SCRATCH_BYTES) return NS_ERR_WORKSPACE_TOO_SMALL;
+  void* scratch = nullptr;
+  if (const int rc = ns::noalloc_scratch(&scratch)) return rc;
+  // The kernel zeroes the counts it accumulates in the scratch and writes the
+  // column and value arrays before reading them, so nothing is cleared here.
+  return ns_sample(logits, dtype, batch, vocab, row_stride, hist_ids, hist_offsets, max_history, temperature,
+                   top_k, top_p, repetition_penalty, presence_penalty, frequency_penalty, uniforms, philox_seed,
+                   philox_offset, out_ids, scratch, NS_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+}  // extern "C"
