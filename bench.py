@@ -646,6 +646,34 @@ def run_decode(args, world, rank, local):
                 x = out.logits[:, -1, :]
         return hist
 
+    def generate_device(n_steps, timed):
+        """The same loop with the histories on the device: DeviceBatch reads
+        them from a DeviceHistory and ns_hist_append adds each step's ids --
+        no host lists, no per-step .tolist(); the ids feed the next step
+        directly."""
+        from b200_sampler.sampler import DeviceBatch, DeviceHistory
+        dh = DeviceHistory([list(map(int, r)) for r in prompt], dev, reserve_steps=n_steps + 2)
+        db = DeviceBatch(None, params, dev, seed=5 + rank, history=dh)
+        nxt = torch.empty(B, dtype=torch.int64, device=dev)
+        ids = prompt.to(dev)
+        with torch.inference_mode():
+            out = model(input_ids=ids, use_cache=True)
+            pkv = out.past_key_values
+            x = out.logits[:, -1, :]
+            for t in range(n_steps + 1):
+                if timed:
+                    e_s[t].record()
+                assert db.launch(x, nxt, offset=t) == 0
+                dh.append(nxt)
+                if timed:
+                    e_e[t].record()
+                if t == n_steps:
+                    break
+                out = model(input_ids=nxt[:, None].clone(), past_key_values=pkv, use_cache=True)
+                pkv = out.past_key_values
+                x = out.logits[:, -1, :]
+        return dh
+
     generate(4, False)                                   # warm-up
     torch.cuda.synchronize(dev)
     barrier(world)
@@ -655,6 +683,17 @@ def run_decode(args, world, rank, local):
     dt = time.perf_counter() - t0
     sampler_ms = sum(a.elapsed_time(b) for a, b in zip(e_s, e_e))
     dt = max_over_ranks(world, dt)
+
+    generate_device(4, False)                            # warm-up
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    t0 = time.perf_counter()
+    dh = generate_device(steps, True)
+    torch.cuda.synchronize(dev)
+    dt_dev = max_over_ranks(world, time.perf_counter() - t0)
+    sampler_ms_dev = sum(a.elapsed_time(b) for a, b in zip(e_s, e_e))
+    dev_lists = dh.to_lists()
+    assert min(min(r[P:]) for r in dev_lists) >= 0, "a device-history step reported a failed row"
     line = {"metric": "end-to-end decode tokens/sec, Qwen3-0.6B shape (BASELINE config 5)",
             "value": B * world * (steps + 1) / dt, "unit": UNIT, "n_gpus": world, "steps": steps,
             "warmup": 4, "ms_per_step": dt / (steps + 1) * 1e3, "higher_is_better": True, "scaling": "weak",
@@ -667,7 +706,13 @@ def run_decode(args, world, rank, local):
                         "ms_per_call": sampler_ms / (steps + 1),
                         "note": "CUDA events around select_batch_tensor (host packing of the growing "
                                 "histories, H2D, the kernel)"},
-            "tokens_generated_per_row": len(hist[0]) - P}
+            "tokens_generated_per_row": len(hist[0]) - P,
+            "device_history": {
+                "value": B * world * (steps + 1) / dt_dev, "unit": UNIT, "ms_per_step": dt_dev / (steps + 1) * 1e3,
+                "sampler_ms_total": sampler_ms_dev, "sampler_share_of_step_time": sampler_ms_dev / 1e3 / dt_dev,
+                "sampler_ms_per_call": sampler_ms_dev / (steps + 1),
+                "note": "DeviceBatch + DeviceHistory: histories stay on the device (ns_hist_append per step), "
+                        "ids feed the next step without .tolist(); CUDA events around the launch and the append"}}
     if rank == 0:
         print(json.dumps(line), flush=True)
 

@@ -117,6 +117,25 @@ int ns_sample(const void* logits, int dtype, int64_t batch, int64_t vocab, int64
               int64_t* out_ids, void* workspace, size_t workspace_bytes, ns_stream_t stream);
 
 /*
+ * Device-resident token histories for a decode loop: append each row's
+ * sampled id to its history without a host round trip.
+ * Replaces: the host-side history rebuild of the reference -- prompt +
+ *   outputs lists built per step (engine/context_builder.py:208-213), the new
+ *   id appended to the outputs (driver/output_processor.py:46) -- which
+ *   select_batch then re-uploads.
+ * Input: the CSR history (hist_ids int32, hist_offsets int64 [batch + 1]; both
+ * NULL for empty histories) and new_ids int64 [batch] (ns_sample's out_ids).
+ * Output (other buffers than the input): the same rows each followed by its
+ * new id: out_hist_offsets[b] = hist_offsets[b] + b, out_hist_ids of
+ * hist_offsets[batch] + batch elements.  out_capacity: elements out_hist_ids
+ * holds; the caller sizes it (nothing past it is written).  A negative new id
+ * (a failed row) is stored as -1, which the next ns_sample reports as
+ * NS_ERR_TOKEN_ID_OUT_OF_RANGE for that row.
+ */
+int ns_hist_append(const int32_t* hist_ids, const int64_t* hist_offsets, int64_t batch, const int64_t* new_ids,
+                   int32_t* out_hist_ids, int64_t* out_hist_offsets, int64_t out_capacity, ns_stream_t stream);
+
+/*
  * ns_sample for callers that cannot allocate device memory.  No counterpart
  * in the reference: it is an addition of this library.
  *

@@ -57,6 +57,10 @@ PROTOTYPES = {
         _c_vp, _c_u64, _c_u64,                       # uniforms, philox_seed, philox_offset
         _c_vp, _c_vp,                                # out_ids, stream
     ]),
+    "ns_hist_append": (_c_int, [
+        _c_vp, _c_vp, _c_i64, _c_vp,                 # hist_ids, hist_offsets, batch, new_ids
+        _c_vp, _c_vp, _c_i64, _c_vp,                 # out_hist_ids, out_hist_offsets, out_capacity, stream
+    ]),
     "ns_vp_record_int64s": (_c_int, [_c_i64, _c_int, ctypes.POINTER(_c_i64)]),
     "ns_vp_local": (_c_int, [
         _c_vp, _c_int, _c_i64, _c_i64, _c_i64,       # logits, dtype, batch, vocab_local, row_stride

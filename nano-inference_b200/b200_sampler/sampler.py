@@ -347,13 +347,20 @@ class DeviceBatch:
     must not overlap on the device."""
 
     def __init__(self, histories: Optional[Sequence[Sequence[int]]], params, device,
-                 uniforms: Optional[torch.Tensor] = None, seed: int = 0):
+                 uniforms: Optional[torch.Tensor] = None, seed: int = 0,
+                 history: Optional["DeviceHistory"] = None):
         self.lib = _lib.load()
         self.device = torch.device(device)
         self.batch = len(params)
         self.params = torch.from_numpy(pack_params(params)).to(self.device)      # [6, B]
         self.seed = seed
+        self.history = history   # a DeviceHistory replaces `histories` when given
         B = self.batch
+        if history is not None:
+            if histories is not None:
+                raise ValueError("pass histories or a DeviceHistory, not both")
+            if history.batch != B:
+                raise AssertionError("batch size mismatch (history)")
         if histories is not None and any(len(h) for h in histories):
             lens = np.array([len(h) for h in histories], dtype=np.int64)
             offs = np.zeros(B + 1, dtype=np.int64)
@@ -383,11 +390,94 @@ class DeviceBatch:
         assert B == self.batch and logits.stride(1) == 1 and out.numel() >= B
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
         p = self.params.data_ptr()
-        ws_ptr, ws_bytes = self.workspace.acquire(B, V, self.max_history if self.hist_ids is not None else 0)
+        if self.history is not None:
+            h = self.history
+            hist_ids, hist_offsets, max_h = h.ids.data_ptr(), h.offsets.data_ptr(), h.max_history
+        elif self.hist_ids is not None:
+            hist_ids, hist_offsets, max_h = self.hist_ids.data_ptr(), self.hist_offsets.data_ptr(), self.max_history
+        else:
+            hist_ids, hist_offsets, max_h = None, None, 0
+        ws_ptr, ws_bytes = self.workspace.acquire(B, V, max_h)
         return self.lib.ns_sample(
             logits.data_ptr(), _DTYPES[logits.dtype], B, V, int(logits.stride(0)),
-            None if self.hist_ids is None else self.hist_ids.data_ptr(),
-            None if self.hist_offsets is None else self.hist_offsets.data_ptr(),
-            self.max_history, p, p + 4 * B, p + 8 * B, p + 12 * B, p + 16 * B, p + 20 * B,
+            hist_ids, hist_offsets, max_h, p, p + 4 * B, p + 8 * B, p + 12 * B, p + 16 * B, p + 20 * B,
             None if self.uniforms is None else self.uniforms.data_ptr(), self.seed, offset,
             out.data_ptr(), ws_ptr, ws_bytes, s.cuda_stream)
+
+
+class DeviceHistory:
+    """Token histories (prompt + outputs per row) kept on the device for a
+    decode loop.
+
+    The reference rebuilds every row's history on the host each step --
+    ``prompt_token_ids + output_token_ids`` (engine/context_builder.py:208-213),
+    the sampled id appended to the outputs (driver/output_processor.py:46) --
+    and the sampler re-uploads it.  Here the history is a CSR (int32 ids,
+    int64 offsets) in device memory; ``append(ids)`` adds each row's sampled
+    id with one ``ns_hist_append`` launch on the stream: no host work, no
+    synchronisation, so a decode step can be captured in a CUDA graph once the
+    buffers are large enough.  Two buffers alternate (the kernel reads one and
+    writes the other); ``reserve_steps`` appends fit before a buffer grows, and
+    growing allocates (keep it outside graph capture).  A failed row's
+    negative status is appended as -1, which the next sampling step reports
+    as NS_ERR_TOKEN_ID_OUT_OF_RANGE.
+    """
+
+    def __init__(self, histories: Sequence[Sequence[int]], device, reserve_steps: int = 256):
+        self.lib = _lib.load()
+        self.device = torch.device(device)
+        B = len(histories)
+        self.batch = B
+        lens = np.fromiter((len(h) for h in histories), dtype=np.int64, count=B)
+        offs = np.zeros(B + 1, dtype=np.int64)
+        np.cumsum(lens, out=offs[1:])
+        self.total = int(offs[-1])
+        self.max_history = int(lens.max()) if B else 0
+        flat = np.fromiter(itertools.chain.from_iterable(histories), dtype=np.int64, count=self.total)
+        if flat.size and (flat.min() < -(2 ** 31) or flat.max() >= 2 ** 31):
+            raise IndexError(_lib.status_string(_lib.NS_ERR_TOKEN_ID_OUT_OF_RANGE))
+        cap = self.total + B * max(int(reserve_steps), 1)
+        self._ids = [torch.empty(max(cap, 1), dtype=torch.int32, device=self.device) for _ in range(2)]
+        self._offs = [torch.empty(B + 1, dtype=torch.int64, device=self.device) for _ in range(2)]
+        if self.total:
+            self._ids[0][:self.total].copy_(torch.from_numpy(flat.astype(np.int32)))
+        self._offs[0].copy_(torch.from_numpy(offs))
+        self.cur = 0
+
+    @property
+    def ids(self) -> torch.Tensor:
+        """int32 ids of the current CSR (the first ``total`` are valid)."""
+        return self._ids[self.cur]
+
+    @property
+    def offsets(self) -> torch.Tensor:
+        """int64 [batch + 1] row offsets of the current CSR."""
+        return self._offs[self.cur]
+
+    def append(self, new_ids: torch.Tensor, stream: Optional[torch.cuda.Stream] = None) -> None:
+        """Append new_ids[b] (int64 [batch] on the device, e.g. the sampler's
+        output) to row b, asynchronously on `stream`."""
+        B = self.batch
+        if new_ids.dtype != torch.int64 or new_ids.numel() < B or not new_ids.is_cuda:
+            raise ValueError("new_ids must be an int64 device tensor with one id per row")
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        nxt = 1 - self.cur
+        need = self.total + B
+        if self._ids[nxt].numel() < need:
+            with torch.cuda.stream(s):
+                self._ids[nxt] = torch.empty(max(need, 2 * self._ids[nxt].numel()), dtype=torch.int32,
+                                             device=self.device)
+        rc = self.lib.ns_hist_append(self._ids[self.cur].data_ptr(), self._offs[self.cur].data_ptr(), B,
+                                     new_ids.data_ptr(), self._ids[nxt].data_ptr(), self._offs[nxt].data_ptr(),
+                                     self._ids[nxt].numel(), s.cuda_stream)
+        if rc != _lib.NS_OK:
+            raise RuntimeError(f"ns_hist_append failed: {_lib.status_string(rc)}")
+        self.cur = nxt
+        self.total = need
+        self.max_history += 1
+
+    def to_lists(self) -> List[List[int]]:
+        """The histories as Python lists (synchronises; for checking)."""
+        ids = self.ids[:self.total].cpu().tolist()
+        offs = self.offsets.cpu().tolist()
+        return [ids[offs[b]:offs[b + 1]] for b in range(self.batch)]

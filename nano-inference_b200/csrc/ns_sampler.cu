@@ -4819,6 +4819,59 @@ int ns_ipc_close(void* ptr) {
 }  // extern "C"
 
 // ---------------------------------------------------------------------------
+// Device-resident histories: append one sampled id per row
+// ---------------------------------------------------------------------------
+// The reference rebuilds every row's history as prompt + outputs lists on the
+// host each step (engine/context_builder.py:208-213, outputs appended at
+// driver/output_processor.py:46).  Here the history CSR stays on the device:
+// after a sampling step, row b's ids are copied to out at offset
+// offsets[b] + b and the row's new id follows them, so out_offsets[b] =
+// offsets[b] + b.  One CTA per row (grid-stride over rows beyond the grid);
+// writes past out_capacity elements are dropped (a caller that sized out too
+// small gets a truncated history, never a stray write).
+namespace ns {
+
+constexpr int kAppendThreads = 256;
+
+__global__ void __launch_bounds__(kAppendThreads) hist_append_kernel(const int32_t* __restrict__ ids,
+                                                                     const int64_t* __restrict__ offsets,
+                                                                     int64_t batch, const int64_t* __restrict__ new_ids,
+                                                                     int32_t* __restrict__ out_ids,
+                                                                     int64_t* __restrict__ out_offsets,
+                                                                     int64_t out_capacity) {
+  for (int64_t b = blockIdx.x; b < batch; b += gridDim.x) {
+    const int64_t h0 = offsets ? offsets[b] : 0, h1 = offsets ? offsets[b + 1] : 0;
+    const int64_t dst = h0 + b;
+    for (int64_t i = h0 + threadIdx.x; i < h1; i += kAppendThreads)
+      if (i + b < out_capacity) out_ids[i + b] = ids[i];
+    if (threadIdx.x == 0) {
+      // an error status (negative) is stored as is: the next sampling step
+      // reports NS_ERR_TOKEN_ID_OUT_OF_RANGE for that row
+      const int64_t v = new_ids[b];
+      const int32_t id = (v >= 0 && v <= INT32_MAX) ? int32_t(v) : int32_t(-1);
+      if (dst + (h1 - h0) < out_capacity) out_ids[dst + (h1 - h0)] = id;
+      out_offsets[b] = dst;
+      if (b == batch - 1) out_offsets[batch] = h1 + batch;
+    }
+  }
+}
+
+}  // namespace ns
+
+extern "C" int ns_hist_append(const int32_t* hist_ids, const int64_t* hist_offsets, int64_t batch,
+                              const int64_t* new_ids, int32_t* out_hist_ids, int64_t* out_hist_offsets,
+                              int64_t out_capacity, ns_stream_t stream) {
+  if (batch < 0 || out_capacity < 0) return NS_ERR_INVALID_ARGUMENT;
+  if ((hist_ids == nullptr) != (hist_offsets == nullptr)) return NS_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return NS_OK;
+  if (!new_ids || !out_hist_ids || !out_hist_offsets || out_capacity < batch) return NS_ERR_INVALID_ARGUMENT;
+  const unsigned grid = unsigned(std::min<int64_t>(batch, 65535));
+  ns::hist_append_kernel<<<grid, ns::kAppendThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      hist_ids, hist_offsets, batch, new_ids, out_hist_ids, out_hist_offsets, out_capacity);
+  return cudaGetLastError() == cudaSuccess ? NS_OK : NS_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------------------
 // ns_sample without a caller workspace
 // ---------------------------------------------------------------------------
 // For callers that may not allocate device memory around a sampling step (an

@@ -83,3 +83,13 @@ def test_package_has_no_oracle_dependency():
     for f in glob.glob(os.path.join(pkg, "*.py")):
         src = open(f).read()
         assert not re.search(r"^\s*(from\s+oracle|import\s+oracle)", src, flags=re.M), f
+
+
+def test_hist_append_argument_validation_without_gpu():
+    lib = _lib.load()
+    f = lib.ns_hist_append
+    assert f(None, None, -1, 1, 1, 1, 8, None) == _lib.NS_ERR_INVALID_ARGUMENT
+    assert f(1, None, 2, 1, 1, 1, 8, None) == _lib.NS_ERR_INVALID_ARGUMENT      # ids without offsets
+    assert f(None, None, 2, None, 1, 1, 8, None) == _lib.NS_ERR_INVALID_ARGUMENT  # no new ids
+    assert f(None, None, 4, 1, 1, 1, 3, None) == _lib.NS_ERR_INVALID_ARGUMENT     # capacity below batch
+    assert f(None, None, 0, None, None, None, 0, None) == _lib.NS_OK              # empty batch
