@@ -7,7 +7,7 @@ Headline workload: B=256 rows x V=151936 fp32 logits ``randn*3``, T=0.7,
 top-k 50, top-p 0.9, repetition 1.1, presence 0.5, frequency 0.3, 1024
 uniform history ids per row, one caller uniform per row (synthetic, seeded;
 the reference publishes no benchmark data).  ``--workload`` selects the other
-BASELINE configurations and modes (``b200_sampler.workloads.WORKLOADS``).
+benchmark configurations and modes (``b200_sampler.workloads.WORKLOADS``).
 
 One step = one ``ns_sample`` launch over the batch.  With N GPUs the one
 batch is sharded by rows (strong scaling: rank r samples rows
@@ -469,7 +469,7 @@ def run_ours(args, world, rank, local):
 
 
 def run_vp(args, world, rank, local):
-    """vocab-parallel sampling, B=128 rows of V=151936 fp32
+    """Benchmark configuration 4: vocab-parallel sampling, B=128 rows of V=151936 fp32
     split into `world` contiguous slices; per step ns_vp_local on this rank's
     slice, then the exchange of the candidate records -- `peer`: ns_vp_signal
     and ns_vp_merge_peers, which reads every rank's record in place over
@@ -568,7 +568,7 @@ def run_vp(args, world, rank, local):
     ms_per_step = ms / args.steps
     peak, peak_kind = _peaks()
     local_bytes = B * width * 4
-    line = {"metric": "vocab-parallel sampled tokens/sec at B=128,V=151936 (BASELINE config 4)",
+    line = {"metric": "vocab-parallel sampled tokens/sec at B=128,V=151936 (benchmark configuration 4)",
             "value": B / (ms_per_step / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded randn*3 logits)",
@@ -591,7 +591,7 @@ def run_vp(args, world, rank, local):
 
 
 def run_decode(args, world, rank, local):
-    """an end-to-end decode loop.  A Qwen3-0.6B-shaped
+    """Benchmark configuration 5: an end-to-end decode loop.  A Qwen3-0.6B-shaped
     model (28 layers, hidden 1024, 16 query / 8 KV heads, head_dim 128,
     vocab 151936; transformers' Qwen3 with random-init bf16 weights), batch
     64, 128-token random prompts, 256 decode steps, each sampled through
@@ -694,7 +694,7 @@ def run_decode(args, world, rank, local):
     sampler_ms_dev = sum(a.elapsed_time(b) for a, b in zip(e_s, e_e))
     dev_lists = dh.to_lists()
     assert min(min(r[P:]) for r in dev_lists) >= 0, "a device-history step reported a failed row"
-    line = {"metric": "end-to-end decode tokens/sec, Qwen3-0.6B shape (BASELINE config 5)",
+    line = {"metric": "end-to-end decode tokens/sec, Qwen3-0.6B shape (benchmark configuration 5)",
             "value": B * world * (steps + 1) / dt, "unit": UNIT, "n_gpus": world, "steps": steps,
             "warmup": 4, "ms_per_step": dt / (steps + 1) * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, random prompts)",

@@ -1,4 +1,4 @@
-"""Parity at the exact shapes the benchmark and the BASELINE configurations
+"""Parity at the exact shapes the benchmark and the benchmark configurations
 run, through the C ABI, against the CPU oracle.
 
 The launch shape depends on the batch: from 148 rows up (the SM count) every

@@ -106,7 +106,7 @@ def test_vp_matches_whole_rows_and_oracle(dtype, split):
 
 
 def test_vp_config4_eight_slices():
-    """128 rows, 8 slices of 18992, k 50, p 0.95, T 0.8."""
+    """Benchmark configuration 4: 128 rows, 8 slices of 18992, k 50, p 0.95, T 0.8."""
     B, V = 128, 151936
     x = make_logits(4, B, V, 3.0)
     params = [SamplingParams(temperature=0.8, top_k=50, top_p=0.95)] * B
