@@ -82,6 +82,18 @@ int ns_sampler_workspace_bytes(int64_t batch, int64_t vocab, int64_t max_history
                                size_t* out_bytes);
 
 /*
+ * Dynamic shared memory per block that ns_sample uses for this problem on a
+ * device with sm_count SMs (a row with a history; no device needed): the
+ * launch's own geometry and layout arithmetic.  It does not grow with
+ * max_history -- a block keeps at most 1024 distinct history ids in shared
+ * memory and the rest go to the workspace -- so two blocks fit an SM at any
+ * history length (about 111 KB at vocab 151936, batch 256, 148 SMs).
+ * Replaces: nothing (a sizing query).
+ */
+int ns_sampler_smem_bytes(int dtype, int64_t batch, int64_t vocab, int64_t max_history, int sm_count,
+                          size_t* out_bytes);
+
+/*
  * Sample one token per row.
  * Replaces: Sampler.select_batch (sampler.py:36-91), including
  *   _apply_repetition_penalty (sampler.py:93-108), greedy argmax (:60-70),

@@ -41,6 +41,7 @@ PROTOTYPES = {
     "ns_status_string": (ctypes.c_char_p, [_c_int]),
     "ns_version": (_c_int, []),
     "ns_sampler_workspace_bytes": (_c_int, [_c_i64, _c_i64, _c_i64, ctypes.POINTER(_c_sz)]),
+    "ns_sampler_smem_bytes": (_c_int, [_c_int, _c_i64, _c_i64, _c_i64, _c_int, ctypes.POINTER(_c_sz)]),
     "ns_sample": (_c_int, [
         _c_vp, _c_int, _c_i64, _c_i64, _c_i64,       # logits, dtype, batch, vocab, row_stride
         _c_vp, _c_vp, _c_i64,                        # hist_ids, hist_offsets, max_history

@@ -4575,6 +4575,29 @@ int ns_sampler_workspace_bytes(int64_t batch, int64_t vocab, int64_t max_history
   return NS_OK;
 }
 
+int ns_sampler_smem_bytes(int dtype, int64_t batch, int64_t vocab, int64_t max_history, int sm_count,
+                          size_t* out_bytes) {
+  if (!out_bytes || batch <= 0 || vocab <= 0 || max_history < 0 || sm_count <= 0) return NS_ERR_INVALID_ARGUMENT;
+  if (vocab > (int64_t(1) << 24) || batch > (int64_t(1) << 24)) return NS_ERR_INVALID_ARGUMENT;
+  if (dtype != NS_DTYPE_F32 && dtype != NS_DTYPE_BF16 && dtype != NS_DTYPE_F16) return NS_ERR_UNSUPPORTED_DTYPE;
+  // the arithmetic of launch(): geometry, then the shared-memory layout of a
+  // row with a history (the bitmap, prefixes and rank arrays present)
+  auto size = [&](auto geom, int te) {
+    const ns::Geom g = geom;
+    const int64_t tpw = (g.pw + te - 1) / te;
+    const int nwords = max_history > 0 ? int((g.span + 31) / 32) : 0;
+    const int cnt_cap = max_history > 0 ? int(std::min<int64_t>(ns::hist_cap(max_history, g), ns::kHistSmem)) : 0;
+    return size_t(ns::make_layout(nwords, cnt_cap, int(ns::kWarps * tpw)).total);
+  };
+  if (dtype == NS_DTYPE_F32)
+    *out_bytes = size(ns::geometry<NS_DTYPE_F32>(batch, vocab, sm_count), ns::Ctx<NS_DTYPE_F32>::TE);
+  else if (dtype == NS_DTYPE_BF16)
+    *out_bytes = size(ns::geometry<NS_DTYPE_BF16>(batch, vocab, sm_count), ns::Ctx<NS_DTYPE_BF16>::TE);
+  else
+    *out_bytes = size(ns::geometry<NS_DTYPE_F16>(batch, vocab, sm_count), ns::Ctx<NS_DTYPE_F16>::TE);
+  return NS_OK;
+}
+
 int ns_sample(const void* logits, int dtype, int64_t batch, int64_t vocab, int64_t row_stride,
               const int32_t* hist_ids, const int64_t* hist_offsets, int64_t max_history,
               const float* temperature, const int32_t* top_k, const float* top_p,

@@ -93,3 +93,22 @@ def test_hist_append_argument_validation_without_gpu():
     assert f(None, None, 2, None, 1, 1, 8, None) == _lib.NS_ERR_INVALID_ARGUMENT  # no new ids
     assert f(None, None, 4, 1, 1, 1, 3, None) == _lib.NS_ERR_INVALID_ARGUMENT     # capacity below batch
     assert f(None, None, 0, None, None, None, 0, None) == _lib.NS_OK              # empty batch
+
+
+def test_shared_memory_does_not_grow_with_the_history():
+    """Two blocks per SM at any history length: the per-block shared memory
+    of the headline shape (vocab 151936, batch 256, a 148-SM B200) is the same
+    from 1024 to 32768 history ids and leaves room for a second block
+    (228 KB per SM, 1 KB of it reserved per block)."""
+    lib = _lib.load()
+    sz = ctypes.c_size_t()
+    sizes = {}
+    for h in (1024, 2048, 11000, 12000, 32768):
+        assert lib.ns_sampler_smem_bytes(_lib.NS_DTYPE_F32, 256, 151936, h, 148, ctypes.byref(sz)) == _lib.NS_OK
+        sizes[h] = sz.value
+    assert len(set(sizes.values())) == 1, sizes
+    assert 2 * (sizes[1024] + 1024) <= 228 * 1024, sizes
+    assert lib.ns_sampler_smem_bytes(_lib.NS_DTYPE_F32, 256, 151936, 0, 148, ctypes.byref(sz)) == _lib.NS_OK
+    assert sz.value <= sizes[1024]                    # no history: no bitmap or rank arrays
+    assert lib.ns_sampler_smem_bytes(7, 256, 151936, 0, 148, ctypes.byref(sz)) == _lib.NS_ERR_UNSUPPORTED_DTYPE
+    assert lib.ns_sampler_smem_bytes(0, 0, 151936, 0, 148, ctypes.byref(sz)) == _lib.NS_ERR_INVALID_ARGUMENT
