@@ -14,7 +14,7 @@ batch is sharded by rows (strong scaling: rank r samples rows
 [r B / N, (r + 1) B / N)); a second, labelled measurement gives every rank the
 full batch (weak scaling).  ``value`` is sampled tokens/s of the whole batch
 with inputs resident in HBM: CUDA-graph replays of exactly K launches that
-rotate over 3 logits buffers (> the 126 MB L2 at the headline), timed with
+rotate over logits buffers totalling >= 2x the L2 (3 at the headline), timed with
 CUDA events on the launching stream and bracketed by a barrier and a device
 synchronisation; the K-step region is repeated until >= 1 s has elapsed and
 the median repeat (max over ranks) is reported.  ``e2e`` is the same metric
@@ -52,7 +52,19 @@ import torch  # noqa: E402
 
 METRIC = "sampled tokens/sec and logits HBM GB/s vs peak at B=256,V=151936"
 UNIT = "tokens/s"
-N_BUFFERS = 3
+N_BUFFERS = 3          # at least this many rotating logits buffers ...
+L2_MULTIPLE = 2        # ... and together at least this many times the device's L2
+
+
+def n_buffers(dev, bytes_per_buffer: int) -> int:
+    """Rotating input buffers whose total is >= L2_MULTIPLE x the L2, so no
+    timed launch finds its logits in L2 (a small per-GPU shard would
+    otherwise fit it)."""
+    import math
+    l2 = int(getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 << 20))
+    return max(N_BUFFERS, int(math.ceil(L2_MULTIPLE * l2 / max(bytes_per_buffer, 1))))
+
+
 GRAPH_LAUNCHES = 500
 MIN_TIMED_S = 1.0
 REF_BUDGET_S = 60.0
@@ -319,13 +331,15 @@ def timed_repeats(world, dev, stream, run_k):
 def measure_rows(args, world, dev, w, r0, r1, clk=None):
     """Device time per step of ns_sample over rows [r0, r1) of workload w:
     warm-up launches, then CUDA graphs of exactly K launches rotating over
-    N_BUFFERS logits buffers.  Returns (median ms per step, repeats, ids of
-    the first launch on the unrotated logits)."""
+    logits buffers totalling >= L2_MULTIPLE x the L2.  Returns (median ms per
+    step, repeats, ids of the first launch on the unrotated logits, (graph
+    launches, replays, remainder, buffers))."""
     from b200_sampler.sampler import DeviceBatch
     rows = slice(r0, r1)
     db = DeviceBatch(w.histories[r0:r1], w.params[r0:r1], dev, uniforms=w.uniforms[rows])
     base = w.logits[rows]
-    bufs = [base.to(dev)] + [base.roll(i, dims=1).to(dev) for i in range(1, N_BUFFERS)]
+    nb = n_buffers(dev, base.numel() * base.element_size())
+    bufs = [base.to(dev)] + [base.roll(i, dims=1).to(dev) for i in range(1, nb)]
     out = torch.empty(r1 - r0, dtype=torch.int64, device=dev)
     stream = torch.cuda.Stream(dev)
     with torch.cuda.stream(stream):
@@ -335,14 +349,14 @@ def measure_rows(args, world, dev, w, r0, r1, clk=None):
     first_ids = out.cpu().tolist()
     with torch.cuda.stream(stream):
         for i in range(max(args.warmup, 3)):
-            assert db.launch(bufs[i % N_BUFFERS], out, stream) == 0
+            assert db.launch(bufs[i % nb], out, stream) == 0
     stream.synchronize()
 
     def capture(n):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             for i in range(n):
-                db.launch(bufs[i % N_BUFFERS], out, torch.cuda.current_stream(dev))
+                db.launch(bufs[i % nb], out, torch.cuda.current_stream(dev))
         return g
     per = min(args.steps, GRAPH_LAUNCHES)
     reps, rem = divmod(args.steps, per)
@@ -363,7 +377,7 @@ def measure_rows(args, world, dev, w, r0, r1, clk=None):
     else:
         ms, all_ms = timed_repeats(world, dev, stream, run_k)
     del g, g_rem
-    return ms / args.steps, [m / args.steps for m in all_ms], first_ids, (per, reps, rem)
+    return ms / args.steps, [m / args.steps for m in all_ms], first_ids, (per, reps, rem, nb)
 
 
 def run_e2e(args, world, w, dev, r0, r1):
@@ -402,7 +416,7 @@ def run_ours(args, world, rank, local):
     esz = w.logits.element_size()
     r0, r1 = rank * B // world, (rank + 1) * B // world
     clk = ClockSampler(local)
-    ms_step, all_ms, first_ids, (per, reps, rem) = measure_rows(args, world, dev, w, r0, r1, clk)
+    ms_step, all_ms, first_ids, (per, reps, rem, nb) = measure_rows(args, world, dev, w, r0, r1, clk)
     tokens_per_s = B / (ms_step / 1e3)
     # roofline of the dominant kernel: algorithmic bytes of the rows this
     # rank launched over the launch's average device time (max over ranks)
@@ -428,8 +442,8 @@ def run_ours(args, world, rank, local):
             "config": {"workload": w.notes, "name": args.workload, "global_batch": B, "rows_per_gpu": r1 - r0,
                        "vocab": V,
                        "parallelism": f"one batch sharded by rows over {world} GPU(s), no collective",
-                       "l2": f"{N_BUFFERS} rotating logits buffers ({N_BUFFERS * (r1 - r0) * V * esz / 1e6:.0f} MB "
-                             f"per GPU; > the 126 MB L2 when above it)",
+                       "l2": f"{nb} rotating logits buffers ({nb * (r1 - r0) * V * esz / 1e6:.0f} MB per GPU, "
+                             f">= {L2_MULTIPLE}x the L2): no timed launch finds its logits in L2",
                        "timing": f"CUDA graphs ({per} launches x {reps} replays{f' + {rem}' if rem else ''}) "
                                  f"= K steps per repeat, {len(all_ms)} repeats >= {MIN_TIMED_S:.0f} s, median "
                                  f"repeat, CUDA events, max over ranks",
@@ -488,8 +502,9 @@ def run_vp(args, world, rank, local):
     off = rank * w
     width = min(w, V - off)
     full = make_logits(0, B, V, 3.0)
+    nb = n_buffers(dev, B * width * 4)   # this rank's slices, >= L2_MULTIPLE x the L2 in total
     bufs = [full[:, off:off + width].contiguous().to(dev)]
-    for i in range(1, N_BUFFERS):
+    for i in range(1, nb):
         bufs.append(full.roll(i, dims=1)[:, off:off + width].contiguous().to(dev))
     params = [SamplingParams(temperature=0.8, top_k=K, top_p=0.95)] * B
     p = torch.from_numpy(pack_params(params)).to(dev)
@@ -513,7 +528,7 @@ def run_vp(args, world, rank, local):
 
     def step(i):
         # step i writes record buffer i % 2: every run of steps alternates
-        x = bufs[i % N_BUFFERS]
+        x = bufs[i % nb]
         rp = ex.record(rank, i & 1) if peer else rec.data_ptr()
         rc = lib.ns_vp_local(x.data_ptr(), _lib.NS_DTYPE_F32, B, width, width, off, V, None, None, 0,
                              pp, pp + 4 * B, pp + 8 * B, None, None, None, cap, rp,
@@ -574,6 +589,8 @@ def run_vp(args, world, rank, local):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded randn*3 logits)",
             "config": {"workload": f"B={B} V={V} fp32 split into {world} slices of <= {w}; T=0.8 k={K} p=0.95",
                        "record_bytes_per_rank": int(n.value) * 8,
+                       "l2": f"{nb} rotating logits slices per GPU ({nb * B * width * 4 / 1e6:.0f} MB, "
+                             f">= {L2_MULTIPLE}x the L2)",
                        "transport": ("peer: records read in place over NVLink by the merge kernel after a "
                                      "flag signal" if peer else "gather: NCCL all-gather of the records"),
                        "timing": f"CUDA graphs of local + exchange + merge ({per} steps x {reps}"
